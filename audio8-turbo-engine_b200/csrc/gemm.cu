@@ -1,0 +1,529 @@
+// tcgen05 GEMM with fused epilogues for the decode tick:  Y = epilogue( X[M,K] . W[N,K]^T ).
+//
+// Layout ("swap AB"): the weight supplies the 128-row UMMA M dimension and the token rows the UMMA N dimension
+// (16..256), so a decode batch of a few dozen rows still fills whole 128-lane tensor-core tiles and every weight
+// byte is read from HBM once per launch. One CTA = 128 weight rows x ntok token rows x a K range:
+//   warp 0 / one lane : TMA producer (128B-swizzled K-major tiles of W and X, a ring of `stages` smem slots)
+//   warp 1 / one lane : MMA issuer (tcgen05.mma kind::f16, fp32 accumulator in TMEM, commit frees a slot)
+//   all 4 warps       : epilogue (tcgen05.ld 32 lanes x 32 columns per warp, staged through smem)
+// Split-K across blockIdx.z writes fp32 partials; the last block of a tile (atomic ticket) adds them in split order
+// (deterministic) and runs the epilogue. Launched with programmatic dependent launch: the weight tiles of the first
+// stages are requested before griddepcontrol.wait, i.e. while the previous kernel is still finishing.
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+#include "gemm.cuh"
+
+namespace a8 {
+
+constexpr int BK = 64;                  // K elements per stage (128 bytes of bf16: one swizzle atom)
+constexpr int TILE_A_BYTES = 128 * BK * 2;
+constexpr int STAGE_PITCH = 132;        // fp32 epilogue staging row pitch (bank-conflict-free float4 reads)
+constexpr int KERNEL_ID_GEMM = 1;
+
+struct EpiCtx {
+  const GemmArgs* a;
+  int n0, m_base;
+};
+
+// ------------------------------------------------------------------------------------------------ epilogues
+// Every epilogue sees one chunk of 32 token columns: stage[j][r] = fp32 result of weight row n0 + r, token m_base + j.
+// Thread t handles token j = t / 4 and the 32 weight rows [32 (t % 4), +32) of the tile.
+template <int KIND>
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, const float* stage, int n0, int mb, int tid) {
+  const int j = tid >> 2, seg = tid & 3;
+  const int m = mb + j;
+  if (m >= a.M) return;
+  const float* src = stage + j * STAGE_PITCH + seg * 32;
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    float4 f = *reinterpret_cast<const float4*>(src + i);
+    v[i] = f.x; v[i + 1] = f.y; v[i + 2] = f.z; v[i + 3] = f.w;
+  }
+  const A8Epilogue& e = a.epi;
+  const int nb = n0 + seg * 32;
+  if constexpr (KIND == A8_EPI_BF16 || KIND == A8_EPI_GELU || KIND == A8_EPI_LSRES) {
+    const __nv_bfloat16* bias = reinterpret_cast<const __nv_bfloat16*>(e.bias);
+    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(a.y) + (size_t)m * a.ldy;
+    float o[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int n = nb + i;
+      float x = v[i];
+      if (bias != nullptr && n < a.N) x += __bfloat162float(bias[n]);
+      if constexpr (KIND == A8_EPI_BF16) {
+        o[i] = x;
+      } else if constexpr (KIND == A8_EPI_GELU) {
+        const float t = bf16r(x);
+        o[i] = 0.5f * t * (1.0f + erff(t * 0.70710678118654752f));
+      } else {
+        const __nv_bfloat16* res = reinterpret_cast<const __nv_bfloat16*>(e.res) + (size_t)m * e.ldres;
+        const __nv_bfloat16* gam = reinterpret_cast<const __nv_bfloat16*>(e.gamma);
+        if (n < a.N) {
+          const float t = bf16r(x);
+          o[i] = __bfloat162float(res[n]) + bf16r(__bfloat162float(gam[n]) * t);
+        } else {
+          o[i] = 0.f;
+        }
+      }
+    }
+    if (nb + 32 <= a.N && ((reinterpret_cast<uintptr_t>(y + nb) & 15) == 0)) {
+      uint4* dst = reinterpret_cast<uint4*>(y + nb);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        dst[q] = make_uint4(pack_bf16(o[8 * q], o[8 * q + 1]), pack_bf16(o[8 * q + 2], o[8 * q + 3]),
+                            pack_bf16(o[8 * q + 4], o[8 * q + 5]), pack_bf16(o[8 * q + 6], o[8 * q + 7]));
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (nb + i < a.N) y[nb + i] = __float2bfloat16_rn(o[i]);
+    }
+  } else if constexpr (KIND == A8_EPI_F32_ROUND) {
+    float* y = reinterpret_cast<float*>(a.y) + (size_t)m * a.ldy;
+    if (nb + 32 <= a.N && ((reinterpret_cast<uintptr_t>(y + nb) & 15) == 0)) {
+      float4* dst = reinterpret_cast<float4*>(y + nb);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        dst[q] = make_float4(bf16r(v[4 * q]), bf16r(v[4 * q + 1]), bf16r(v[4 * q + 2]), bf16r(v[4 * q + 3]));
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (nb + i < a.N) y[nb + i] = bf16r(v[i]);
+    }
+  }
+}
+
+// SiLU-mul: the tile's rows 0..63 are gate rows g_c, rows 64..127 the matching up rows u_c (c = 64 * tile + i).
+__device__ __forceinline__ void epilogue_silu(const GemmArgs& a, const float* stage, int tile, int mb, int tid) {
+  const int j = tid >> 2, seg = tid & 3;
+  const int m = mb + j;
+  if (m >= a.M) return;
+  const float* g = stage + j * STAGE_PITCH + seg * 16;
+  const float* u = g + 64;
+  const int c0 = tile * 64 + seg * 16;
+  const int I = a.N / 2;
+  __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(a.y) + (size_t)m * a.ldy;
+  float o[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float gv = bf16r(g[i]);
+    const float uv = bf16r(u[i]);
+    const float gs = bf16r(gv / (1.0f + expf(-gv)));
+    o[i] = gs * uv;
+  }
+  if (c0 + 16 <= I && ((reinterpret_cast<uintptr_t>(y + c0) & 15) == 0)) {
+    uint4* dst = reinterpret_cast<uint4*>(y + c0);
+    dst[0] = make_uint4(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]), pack_bf16(o[4], o[5]), pack_bf16(o[6], o[7]));
+    dst[1] = make_uint4(pack_bf16(o[8], o[9]), pack_bf16(o[10], o[11]), pack_bf16(o[12], o[13]),
+                        pack_bf16(o[14], o[15]));
+  } else {
+    for (int i = 0; i < 16; ++i)
+      if (c0 + i < I) y[c0 + i] = __float2bfloat16_rn(o[i]);
+  }
+}
+
+// RoPE: the fused row of token m is [q heads | k heads | v heads] x hd. rotate_half pairs dims (d, d + hd/2), which
+// sit 32 (hd 64) or 64 (hd 128) tile rows apart: the partner of 32-row segment seg is seg ^ (hd / 64).
+__device__ __forceinline__ void epilogue_rope(const GemmArgs& a, const float* stage, int n0, int mb, int tid) {
+  const int j = tid >> 2, seg = tid & 3;
+  const int m = mb + j;
+  if (m >= a.M) return;
+  const A8Epilogue& e = a.epi;
+  const int hd = e.hd, half = hd >> 1;
+  const int nb = n0 + seg * 32;
+  if (nb >= a.N) return;
+  const int pseg = seg ^ (hd >> 6);
+  const float* src = stage + j * STAGE_PITCH + seg * 32;
+  const float* psrc = stage + j * STAGE_PITCH + pseg * 32;
+  const __nv_bfloat16* bias = reinterpret_cast<const __nv_bfloat16*>(e.bias);
+  const int head = nb / hd;                 // fused head index: q 0..nq-1, k nq..nq+nkv-1, v after
+  const int d0 = nb - head * hd;            // first dim of this segment inside the head
+  const int pos = e.pos[m];
+  const int slot = e.slot != nullptr ? e.slot[m] : m;
+  float o[32];
+  if (head < e.nq + e.nkv) {
+    const __nv_bfloat16* cs = reinterpret_cast<const __nv_bfloat16*>(e.cos) + (size_t)pos * hd;
+    const __nv_bfloat16* sn = reinterpret_cast<const __nv_bfloat16*>(e.sin) + (size_t)pos * hd;
+    const int pb = n0 + pseg * 32;          // partner rows
+    const float sign = d0 < half ? -1.0f : 1.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float x = bf16r(src[i]);
+      float xp = bf16r(psrc[i]);
+      if (bias != nullptr) {
+        x += __bfloat162float(bias[nb + i]);
+        xp += __bfloat162float(bias[pb + i]);
+      }
+      const float c = __bfloat162float(cs[d0 + i]), s = __bfloat162float(sn[d0 + i]);
+      o[i] = x * c + sign * xp * s;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float x = bf16r(src[i]);
+      if (bias != nullptr) x += __bfloat162float(bias[nb + i]);
+      o[i] = x;
+    }
+  }
+  __nv_bfloat16* dst;
+  if (head < e.nq) {
+    dst = reinterpret_cast<__nv_bfloat16*>(a.y) + (size_t)m * a.ldy + nb;
+  } else {
+    const bool is_k = head < e.nq + e.nkv;
+    const int kh = is_k ? head - e.nq : head - e.nq - e.nkv;
+    const int col = pos % e.ring;
+    __nv_bfloat16* cache = reinterpret_cast<__nv_bfloat16*>(is_k ? e.kc : e.vc);
+    dst = cache + (((size_t)slot * e.nkv + kh) * e.cache_len + col) * hd + d0;
+  }
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    d4[q] = make_uint4(pack_bf16(o[8 * q], o[8 * q + 1]), pack_bf16(o[8 * q + 2], o[8 * q + 3]),
+                       pack_bf16(o[8 * q + 4], o[8 * q + 5]), pack_bf16(o[8 * q + 6], o[8 * q + 7]));
+}
+
+template <int KIND>
+__device__ __forceinline__ void run_epilogue(const GemmArgs& a, const float* stage, int n0, int mb, int tid) {
+  if constexpr (KIND == A8_EPI_SILU) {
+    epilogue_silu(a, stage, n0 / 128, mb, tid);
+  } else if constexpr (KIND == A8_EPI_ROPE) {
+    epilogue_rope(a, stage, n0, mb, tid);
+  } else {
+    epilogue_chunk<KIND>(a, stage, n0, mb, tid);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ kernel
+template <int KIND>
+__global__ void __launch_bounds__(128, 1)
+    k_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const GemmArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int stages = a.stages;
+  const uint32_t stage_bytes = TILE_A_BYTES + a.ntok * BK * 2;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * stage_bytes);
+  uint64_t* empty = full + stages;
+  uint64_t* accum = empty + stages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile_n = blockIdx.x, tile_m = blockIdx.y, split = blockIdx.z;
+  const int n0 = tile_n * 128, m0 = tile_m * a.ntok;
+  const int kb0 = split * a.kb_per_split;
+  const int nkb = min(a.kb_total, kb0 + a.kb_per_split) - kb0;
+
+  if (tid == 0) {
+    tma_prefetch(&tmW);
+    tma_prefetch(&tmX);
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, a.tmem_cols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_launch();
+
+  auto tileA = [&](int s) { return smem + s * stage_bytes; };
+  auto tileB = [&](int s) { return smem + s * stage_bytes + TILE_A_BYTES; };
+
+  int issued = 0;                               // stage loads requested (producer lane)
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pw = policy_evict_first(), px = policy_evict_last();
+      const int pre = min(stages, nkb);
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], stage_bytes);
+        tma_load_2d(tileA(i), &tmW, &full[i], (kb0 + i) * BK, n0, pw);
+      }
+      pdl_wait();                               // X is produced by the previous kernel
+      for (int i = 0; i < pre; ++i) tma_load_2d(tileB(i), &tmX, &full[i], (kb0 + i) * BK, m0, px);
+      issued = pre;
+      for (int i = pre; i < nkb; ++i) {
+        const int s = i % stages;
+        if (!mbar_wait(&empty[s], ((i / stages) - 1) & 1, ERR_TIMEOUT_EMPTY, KERNEL_ID_GEMM)) break;
+        mbar_arrive_expect_tx(&full[s], stage_bytes);
+        tma_load_2d(tileA(s), &tmW, &full[s], (kb0 + i) * BK, n0, pw);
+        tma_load_2d(tileB(s), &tmX, &full[s], (kb0 + i) * BK, m0, px);
+        issued = i + 1;
+      }
+      // every requested stage has landed before the slots are reused as epilogue staging (immediate in normal
+      // operation: the MMA issuer consumed them; bounded after an error)
+      for (int i = max(0, issued - stages); i < issued; ++i)
+        mbar_wait(&full[i % stages], (i / stages) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_GEMM);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc(128, a.ntok, 1);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % stages;
+        if (!mbar_wait(&full[s], (i / stages) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_GEMM)) break;
+        tc_fence_after();
+        const uint64_t da = umma_desc_sw128(tileA(s)), db = umma_desc_sw128(tileB(s));
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (i | k) != 0);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(accum);
+    }
+  }
+  __syncwarp();
+  pdl_wait();
+  const bool ok = mbar_wait(accum, 0, ERR_TIMEOUT_ACCUM, KERNEL_ID_GEMM);
+  __syncthreads();                              // the producer's drain is done before staging reuses the slots
+  tc_fence_after();
+
+  float* stage = reinterpret_cast<float*>(smem);  // the pipeline slots are idle now: 32 x STAGE_PITCH fp32
+  const int row = warp * 32 + lane;
+  const uint32_t trow = tmem + (uint32_t(warp * 32) << 16);
+  const int nchunk = (a.ntok + 31) / 32;
+  const int tiles = a.n_tiles * a.tok_tiles;
+  const int tile = tile_m * a.n_tiles + tile_n;
+
+  if (a.splits == 1) {
+    for (int c = 0; c < nchunk; ++c) {
+      float v[32];
+      tmem_ld32(trow + c * 32, v);
+      if (!ok) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) stage[i * STAGE_PITCH + row] = v[i];
+      __syncthreads();
+      run_epilogue<KIND>(a, stage, n0, m0 + c * 32, tid);
+      __syncthreads();
+    }
+  } else {
+    const int ntok32 = nchunk * 32;
+    float* part = a.ws + ((size_t)split * tiles + tile) * ntok32 * 128;
+    for (int c = 0; c < nchunk; ++c) {
+      float v[32];
+      tmem_ld32(trow + c * 32, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) part[(size_t)(c * 32 + i) * 128 + row] = ok ? v[i] : 0.f;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) *last_flag = (atomicAdd(&a.counters[tile], 1) == a.splits - 1);
+    __syncthreads();
+    if (*last_flag) {
+      __threadfence();
+      for (int c = 0; c < nchunk; ++c) {
+        for (int i = 0; i < 32; ++i) {
+          float s = 0.f;
+          for (int sp = 0; sp < a.splits; ++sp)
+            s += __ldcg(a.ws + (((size_t)sp * tiles + tile) * ntok32 + c * 32 + i) * 128 + row);
+          stage[i * STAGE_PITCH + row] = s;
+        }
+        __syncthreads();
+        run_epilogue<KIND>(a, stage, n0, m0 + c * 32, tid);
+        __syncthreads();
+      }
+      if (tid == 0) a.counters[tile] = 0;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, a.tmem_cols);
+}
+
+// ------------------------------------------------------------------------------------------------ host
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+int encode_map_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                  uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                  CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return A8_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_stride_bytes & 15)) return A8_ERR_ALIGN;
+  if ((uint64_t(box_inner) * elem_bytes) % 16) return A8_ERR_ALIGN;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? A8_OK : A8_ERR_CUDA;
+}
+
+int encode_map_3d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t d0, uint64_t d1,
+                  uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1, uint32_t b2,
+                  CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return A8_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (stride1_bytes & 15) || (stride2_bytes & 15)) return A8_ERR_ALIGN;
+  if ((uint64_t(b0) * elem_bytes) % 16) return A8_ERR_ALIGN;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? A8_OK : A8_ERR_CUDA;
+}
+
+static int pick_ntok(int M) {
+  const int tiles = (M + 255) / 256;
+  int per = (M + tiles - 1) / tiles;
+  return std::max(16, (per + 15) / 16 * 16);
+}
+
+static void shape(int N, int K, int M, int splits_req, int* ntok, int* n_tiles, int* tok_tiles, int* kb_total,
+                  int* kb_per_split, int* splits) {
+  *ntok = pick_ntok(M);
+  *n_tiles = (N + 127) / 128;
+  *tok_tiles = (M + *ntok - 1) / *ntok;
+  *kb_total = (K + BK - 1) / BK;
+  int s = splits_req;
+  if (s <= 0) {
+    const int tiles = *n_tiles * *tok_tiles;
+    s = tiles >= 148 ? 1 : std::max(1, 148 / tiles);
+    s = std::min(s, std::max(1, *kb_total / 2));   // at least two K blocks per split
+  }
+  s = std::min(s, *kb_total);
+  *kb_per_split = (*kb_total + s - 1) / s;
+  *splits = (*kb_total + *kb_per_split - 1) / *kb_per_split;
+}
+
+int gemm_plan(GemmPlan* p, const void* x, int ldx, const void* w, int N, int K, int M, void* y, int ldy,
+              const A8Epilogue* epi, float* ws, long long ws_floats, int* counters, int n_counters, int splits) {
+  std::memset(p, 0, sizeof(*p));
+  if (x == nullptr || w == nullptr || y == nullptr || epi == nullptr || N <= 0 || K <= 0 || M <= 0) return A8_ERR_ARG;
+  if (epi->kind < A8_EPI_BF16 || epi->kind > A8_EPI_LSRES) return A8_ERR_ARG;
+  if (epi->kind == A8_EPI_SILU && (N % 128) != 0) return A8_ERR_ARG;
+  if (epi->kind == A8_EPI_ROPE && (epi->hd != 64 && epi->hd != 128)) return A8_ERR_ARG;
+  if (epi->kind == A8_EPI_ROPE && (N != (epi->nq + 2 * epi->nkv) * epi->hd || epi->pos == nullptr ||
+                                   epi->kc == nullptr || epi->vc == nullptr ||
+                                   epi->cos == nullptr || epi->ring <= 0))
+    return A8_ERR_ARG;
+  if (epi->kind == A8_EPI_LSRES && (epi->res == nullptr || epi->gamma == nullptr)) return A8_ERR_ARG;
+  GemmArgs& a = p->args;
+  shape(N, K, M, splits, &a.ntok, &a.n_tiles, &a.tok_tiles, &a.kb_total, &a.kb_per_split, &a.splits);
+  a.N = N;
+  a.K = K;
+  a.M = M;
+  a.ldy = ldy;
+  a.y = y;
+  a.epi = *epi;
+  a.tmem_cols = a.ntok <= 32 ? 32 : a.ntok <= 64 ? 64 : a.ntok <= 128 ? 128 : 256;
+  const int stage_bytes = TILE_A_BYTES + a.ntok * BK * 2;
+  const int budget = 200 * 1024;
+  a.stages = std::max(2, std::min(8, budget / stage_bytes));
+  a.stages = std::min(a.stages, std::max(2, a.kb_per_split));
+  if (a.splits > 1) {
+    const long long need = (long long)a.splits * a.n_tiles * a.tok_tiles * ((a.ntok + 31) / 32 * 32) * 128;
+    if (ws == nullptr || counters == nullptr || ws_floats < need || n_counters < a.n_tiles * a.tok_tiles)
+      return A8_ERR_SIZE;
+    a.ws = ws;
+    a.counters = counters;
+  }
+  int rc = encode_map_2d(&p->tmW, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N, (uint64_t)K * 2, BK, 128,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_map_2d(&p->tmX, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, (uint64_t)ldx * 2, BK, a.ntok,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  p->grid = dim3(a.n_tiles, a.tok_tiles, a.splits);
+  p->smem_bytes = a.stages * stage_bytes + 1024 + 256;
+  p->kind = epi->kind;
+  p->ok = true;
+  return A8_OK;
+}
+
+template <int KIND>
+static cudaError_t launch_kind(const GemmPlan* p, cudaStream_t s, bool pdl) {
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k_gemm<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    attr = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = p->grid;
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = p->smem_bytes;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k_gemm<KIND>, p->tmW, p->tmX, p->args);
+}
+
+int gemm_launch(const GemmPlan* p, cudaStream_t s, bool pdl) {
+  if (!p->ok) return A8_ERR_ARG;
+  cudaError_t e;
+  switch (p->kind) {
+    case A8_EPI_BF16: e = launch_kind<A8_EPI_BF16>(p, s, pdl); break;
+    case A8_EPI_F32_ROUND: e = launch_kind<A8_EPI_F32_ROUND>(p, s, pdl); break;
+    case A8_EPI_SILU: e = launch_kind<A8_EPI_SILU>(p, s, pdl); break;
+    case A8_EPI_ROPE: e = launch_kind<A8_EPI_ROPE>(p, s, pdl); break;
+    case A8_EPI_GELU: e = launch_kind<A8_EPI_GELU>(p, s, pdl); break;
+    case A8_EPI_LSRES: e = launch_kind<A8_EPI_LSRES>(p, s, pdl); break;
+    default: return A8_ERR_ARG;
+  }
+  return e == cudaSuccess ? A8_OK : A8_ERR_CUDA;
+}
+
+}  // namespace a8
+
+using namespace a8;
+
+extern "C" int a8_gemm_workspace(int N, int K, int M, int splits, long long* ws_floats, int* n_counters) {
+  if (N <= 0 || K <= 0 || M <= 0) return A8_ERR_ARG;
+  int ntok, nt, tt, kbt, kbs, sp;
+  shape(N, K, M, splits, &ntok, &nt, &tt, &kbt, &kbs, &sp);
+  if (ws_floats) *ws_floats = sp > 1 ? (long long)sp * nt * tt * ((ntok + 31) / 32 * 32) * 128 : 0;
+  if (n_counters) *n_counters = sp > 1 ? nt * tt : 0;
+  return A8_OK;
+}
+
+extern "C" int a8_gemm(const void* x, int ldx, const void* w, int N, int K, int M, void* y, int ldy,
+                       const A8Epilogue* epi, float* ws, long long ws_floats, int* counters, int n_counters,
+                       int splits, a8_stream_t stream) {
+  GemmPlan p;
+  int rc = gemm_plan(&p, x, ldx, w, N, K, M, y, ldy, epi, ws, ws_floats, counters, n_counters, splits);
+  if (rc) return rc;
+  return gemm_launch(&p, reinterpret_cast<cudaStream_t>(stream), true);
+}
+
+extern "C" int a8_device_ok(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return 0;
+  return prop.major == 10 && prop.minor == 0;
+}
+
+extern "C" int a8_get_error(int out[4]) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return A8_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(out, g_err, sizeof(int) * 4) != cudaSuccess) return A8_ERR_CUDA;
+  return A8_OK;
+}
+
+extern "C" int a8_clear_error(void) {
+  int z[4] = {0, 0, 0, 0};
+  return cudaMemcpyToSymbol(g_err, z, sizeof(z)) == cudaSuccess ? A8_OK : A8_ERR_CUDA;
+}

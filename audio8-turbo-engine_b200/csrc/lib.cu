@@ -1,0 +1,6 @@
+// libaudio8_b200.so: the whole library as one translation unit (its kernels share the device error record).
+#include "gemm.cu"
+#include "attention.cu"
+#include "rowops.cu"
+#include "sample.cu"
+#include "engine.cu"

@@ -1,0 +1,487 @@
+"""FastEngine: the drop-in for serve/fast_engine.py's FastEngine on a B200.
+
+Same constructor, attributes and methods as the reference (serve/fast_engine.py:570-1156); the worker
+(serve/engine_worker.py) drives it unchanged: ``capture()``, ``admit(slots, reqs)``, ``bucket_for(n)``,
+``replay(b)``, then reads ``tok_in[:b]``, ``audio[:b]`` and ``frame_prev[:b]``.
+
+PyTorch only allocates device memory and provides streams and CUDA graphs here. Every kernel of the tick and of
+admission is a hand-written sm_100a kernel in libaudio8_b200.so, reached through its C ABI (include/audio8_b200.h):
+``a8_tick`` launches one whole frame (fast AR, slow AR, sampling, state update), recorded once per bucket into a
+CUDA graph; ``a8_stack_forward`` + ``a8_prefill_finish`` run the packed prefill of an admission.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+import time
+from types import SimpleNamespace
+from typing import Dict, List
+
+import numpy as np
+import torch
+
+from . import _lib as L
+
+BF16 = torch.bfloat16
+
+
+def permute_qk(w, nq, nkv, hd):
+    """Rows of the fused [q | k | v] projection with every q / k head's dims reordered from interleaved RoPE pairs
+    (2i, 2i+1) to rotate_half halves (i, i + hd/2); q.k is unchanged (serve/fast_engine.py:60-67)."""
+    p = torch.cat([torch.arange(0, hd, 2), torch.arange(1, hd, 2)]).to(w.device)
+    rest = w.shape[1:]
+    q = w[:nq * hd].reshape(nq, hd, *rest)[:, p].reshape(nq * hd, *rest)
+    k = w[nq * hd:(nq + nkv) * hd].reshape(nkv, hd, *rest)[:, p].reshape(nkv * hd, *rest)
+    return torch.cat([q, k, w[(nq + nkv) * hd:]], 0).contiguous()
+
+
+def rope_tables(base, hd, n):
+    """cos / sin [n, hd] (bf16) for rotate_half: fp32 phases rounded to bf16 (serve/fast_engine.py:70-75)."""
+    fr = 1.0 / (base ** (torch.arange(0, hd, 2).float()[: hd // 2] / hd))
+    ph = torch.outer(torch.arange(n).float(), fr)
+    c, s = ph.cos().to(BF16), ph.sin().to(BF16)
+    return torch.cat([c, c], -1).contiguous(), torch.cat([s, s], -1).contiguous()
+
+
+def interleave_w13(w1, w3):
+    """[w1; w3] reordered so each 128-row tile holds 64 gate rows then the 64 matching up rows (the GEMM's SiLU-mul
+    epilogue pairs them inside one tile)."""
+    I, D = w1.shape
+    assert I % 64 == 0
+    return torch.cat([w1.reshape(I // 64, 64, D), w3.reshape(I // 64, 64, D)], 1).reshape(2 * I, D).contiguous()
+
+
+def _clean_text(text: str) -> str:
+    return " ".join(str(text).strip().split())
+
+
+class PackedStack:
+    """One transformer stack's packed weights, caches and RoPE tables on the device + its A8StackDesc."""
+
+    def __init__(self, layers, norm, nq, nkv, hd, eps, rope_base, cache_rows, cache_len, max_pos, dev, ring=0,
+                 layer_scale=False):
+        def w(t):
+            return t.detach().to(torch.float32)
+        wq, bq, wo, w13, w2, l1, l2 = [], [], [], [], [], [], []
+        for Ly in layers:
+            a, f = Ly.attention, Ly.feed_forward
+            o_, d_ = w(a.wo.weight), w(f.w2.weight)
+            if layer_scale:                 # LayerScale folded into the output projections (serve/fast_engine.py:96-98)
+                o_ = o_ * w(Ly.attention_layer_scale.gamma)[:, None]
+                d_ = d_ * w(Ly.ffn_layer_scale.gamma)[:, None]
+            wq.append(permute_qk(w(a.wqkv.weight), nq, nkv, hd).to(BF16))
+            if a.wqkv.bias is not None:
+                bq.append(permute_qk(w(a.wqkv.bias), nq, nkv, hd).to(BF16))
+            wo.append(o_.to(BF16))
+            w13.append(interleave_w13(w(f.w1.weight).to(BF16), w(f.w3.weight).to(BF16)))
+            w2.append(d_.to(BF16))
+            l1.append(w(Ly.attention_norm.weight).to(BF16))
+            l2.append(w(Ly.ffn_norm.weight).to(BF16))
+        st = lambda xs: torch.stack(xs).to(dev).contiguous()
+        self.wqkv, self.wo, self.w13, self.w2 = st(wq), st(wo), st(w13), st(w2)
+        self.bqkv = st(bq) if bq else None
+        self.ln1, self.ln2 = st(l1), st(l2)
+        self.norm = w(norm.weight).to(BF16).to(dev)
+        c, s = rope_tables(rope_base, hd, max_pos)
+        self.cos, self.sin = c.to(dev), s.to(dev)
+        nl = len(layers)
+        self.kc = torch.zeros(nl, cache_rows, nkv, cache_len, hd, dtype=BF16, device=dev)
+        self.vc = torch.zeros_like(self.kc)
+        self.nq, self.nkv, self.hd, self.eps = nq, nkv, hd, float(eps)
+        self.dim = self.wo.shape[1]
+        self.inter = self.w2.shape[2]
+        self.layers, self.cache_rows, self.cache_len, self.ring = nl, cache_rows, cache_len, int(ring or 0)
+        self.desc = L.A8StackDesc(
+            layers=nl, dim=self.dim, nq=nq, nkv=nkv, hd=hd, inter=self.inter, eps=self.eps, wqkv=L.ptr(self.wqkv),
+            bqkv=L.ptr(self.bqkv), wo=L.ptr(self.wo), w13=L.ptr(self.w13), w2=L.ptr(self.w2), ln1=L.ptr(self.ln1),
+            ln2=L.ptr(self.ln2), norm=L.ptr(self.norm), cos=L.ptr(self.cos), sin=L.ptr(self.sin), kc=L.ptr(self.kc),
+            vc=L.ptr(self.vc), cache_rows=cache_rows, cache_len=cache_len, ring=self.ring)
+
+
+class Scratch:
+    """Activation and split-K buffers for up to `rows` token rows of stacks up to `dim` / `inter` wide."""
+
+    def __init__(self, rows, dim, qdim, inter, nkv, hd, max_len, dev, gemm_floats=1 << 24, counters=8192):
+        mk = lambda n: torch.zeros(rows, n, dtype=BF16, device=dev)
+        self.h, self.q, self.o, self.a, self.mlp = mk(dim), mk(qdim), mk(qdim), mk(dim), mk(inter)
+        self.ws = torch.zeros(gemm_floats, dtype=torch.float32, device=dev)
+        self.counters = torch.zeros(counters, dtype=torch.int32, device=dev)
+        n = C.c_longlong()
+        L.check(L.load().a8_attention_workspace(rows, nkv, hd, max_len, C.byref(n), None), "attention workspace")
+        self.attn_ws = torch.zeros(max(1, n.value), dtype=torch.float32, device=dev)
+        self.attn_counters = torch.zeros(rows * nkv, dtype=torch.int32, device=dev)
+        self.desc = L.A8Scratch(
+            h=L.ptr(self.h), q=L.ptr(self.q), o=L.ptr(self.o), a=L.ptr(self.a), mlp=L.ptr(self.mlp), ws=L.ptr(self.ws),
+            ws_floats=self.ws.numel(), counters=L.ptr(self.counters), n_counters=self.counters.numel(),
+            attn_ws=L.ptr(self.attn_ws), attn_ws_floats=self.attn_ws.numel(), attn_counters=L.ptr(self.attn_counters),
+            n_attn_counters=self.attn_counters.numel())
+
+
+class FastEngine:
+    """serve/fast_engine.py:570 on sm_100a kernels. Sampling noise: Philox keyed by `seed` (default from
+    TTS_SEED, else 1234), counted by the engine's tick number."""
+
+    def __init__(self, model, tokenizer, gen_params: dict, max_slots: int = 32, max_seq: int = 2048, buckets=None,
+                 seq_from_env=True, seed=None):
+        if not torch.cuda.is_available():
+            raise L.A8Error("FastEngine needs a CUDA device (B200); there is no CPU fallback")
+        L.load()
+        dev = torch.device("cuda", torch.cuda.current_device())
+        if not L.load().a8_device_ok():
+            raise L.A8Error("libaudio8_b200 kernels need a compute-capability 10.0 GPU (B200)")
+        self.m, self.tokz = model, tokenizer
+        c = self.cfg = model.config
+        self.dev = dev
+        self.dt = BF16
+        self.B = int(max_slots)
+        S = int(os.environ.get("TTS_MAX_SEQ", str(max_seq))) if seq_from_env else int(max_seq)
+        self.S = min(S, int(c.max_seq_len))
+        gp = dict(gen_params or {})
+        self.gp = gp
+        self.eos, self.sb, self.se = int(c.eos_token_id), int(c.semantic_begin_id), int(c.semantic_end_id)
+        self.ncg, self.cbk = int(c.num_codebooks), int(c.codebook_size)
+        self.nsem = self.se - self.sb + 1
+        self.do_sample = bool(gp.get("do_sample", True))
+        self.temperature = max(float(gp.get("temperature", 0.8) or 1.0), 1e-5)
+        tk = gp.get("top_k", 50)
+        self.top_k = int(tk) if tk and int(tk) > 0 else 0
+        self.top_p = float(gp.get("top_p", 0.95)) if gp.get("top_p", 0.95) is not None else 1.0
+        self.ras_p, self.ras_t, self.ras_w = float(c.ras_top_p), max(float(c.ras_temperature), 1e-5), \
+            int(c.ras_window_size)
+        self.max_new = int(gp.get("max_new_tokens", 2048))
+        self.seed = int(seed if seed is not None else os.environ.get("TTS_SEED", "1234"))
+        B, H = self.B, int(c.dim)
+        self.H = H
+        assert int(c.fast_dim) == H and bool(c.norm_fastlayer_input), "fast_project_in / unnormed fast input"
+        self.prefill_tokens = int(os.environ.get("TTS_PREFILL_TOKENS", "8192"))
+        self.pf_rows = min(self.prefill_tokens, int(os.environ.get("TTS_PREFILL_ROWS", "2048")))
+        self.SCR = B
+        self.slow = PackedStack(model.layers, model.norm, c.n_head, c.n_local_heads, c.head_dim, c.norm_eps,
+                                c.rope_base, cache_rows=B + 1, cache_len=self.S, max_pos=self.S, dev=dev)
+        self.fast = PackedStack(model.fast_layers, model.fast_norm, c.fast_n_head, c.fast_n_local_heads,
+                                c.fast_head_dim, c.norm_eps, c.rope_base, cache_rows=B, cache_len=self.ncg,
+                                max_pos=self.ncg, dev=dev)
+        f32 = lambda t: t.detach().to(torch.float32)
+        emb = f32(model.embeddings.weight)
+        self.emb = emb.to(BF16).to(dev)
+        self.cbemb = f32(model.codebook_embeddings.weight).to(BF16).to(dev)
+        self.cb_off = (torch.arange(self.ncg, device=dev) * self.cbk).view(1, -1)
+        nh = self.nh = self.nsem + 1
+        head = torch.zeros(nh, H, dtype=BF16)
+        head[:self.nsem] = emb[self.sb:self.se + 1].to(BF16)
+        head[self.nsem] = emb[self.eos].to(BF16)
+        self.head = head.to(dev)
+        self.fast_emb = f32(model.fast_embeddings.weight).to(BF16).to(dev)
+        self.fast_out = f32(model.fast_output.weight).to(BF16).to(dev)
+        self.sr = int(getattr(c, "codec_sample_rate", 44100))
+        self.up = 2048
+        self.fps = self.sr / self.up
+        codes, _ = model.encode_audio(torch.zeros(1, 1, self.sr, device=model.device))
+        self.sil_frame = codes[0, :, codes.shape[-1] // 2].long().clamp(min=0).to(dev)
+        self.voc = None
+        self.voc_snaps = {}
+        self.voc_prime = False
+
+        # persistent per-slot state (fixed addresses; row B = SCR, prefill padding)
+        i64, i32 = torch.int64, torch.int32
+        self.tok = torch.zeros(B + 1, dtype=i64, device=dev)
+        self.hid = torch.zeros(B + 1, H, dtype=BF16, device=dev)
+        self.cpos = torch.zeros(B + 1, dtype=i32, device=dev)
+        self.prev = torch.zeros(B + 1, self.ras_w, dtype=i64, device=dev)
+        self.nstep = torch.zeros(B + 1, dtype=i32, device=dev)
+        self.tok_in = torch.zeros(B, dtype=i64, device=dev)
+        self.audio = torch.zeros(B, self.up, dtype=torch.float32, device=dev)
+        self.frame_prev = torch.zeros(B, self.ncg, dtype=i64, device=dev)
+        self.tick_ctr = torch.zeros(1, dtype=i64, device=dev)
+        self.tick_id = torch.zeros(1, dtype=i64, device=dev)
+        # tick scratch
+        self.x_fast2 = torch.zeros(2 * B, H, dtype=BF16, device=dev)
+        self.x_fast = torch.zeros(B, H, dtype=BF16, device=dev)
+        self.x_slow = torch.zeros(B, H, dtype=BF16, device=dev)
+        self.codes = torch.zeros(B, self.ncg, dtype=i64, device=dev)
+        self.ld_logits = (max(self.nh, self.cbk) + 3) // 4 * 4
+        self.logits = torch.zeros(max(B, 64), self.ld_logits, dtype=torch.float32, device=dev)
+        self.f_pos = torch.arange(self.ncg, dtype=i32, device=dev).view(-1, 1).repeat(1, 2 * B).contiguous()
+        self.f_pos0 = (torch.arange(2 * B, dtype=i32, device=dev) % 2).contiguous()
+        self.f_slot0 = (torch.arange(2 * B, dtype=i32, device=dev) // 2).contiguous()
+        rows = max(2 * B, self.pf_rows)
+        self.scratch = Scratch(rows, H, self.slow.nq * self.slow.hd, self.slow.inter, self.slow.nkv, self.slow.hd,
+                               self.S, dev)
+        self.pf_pos = torch.zeros(self.pf_rows, dtype=i32, device=dev)
+        self.pf_slot = torch.zeros(self.pf_rows, dtype=i32, device=dev)
+        self.pf_last = torch.zeros(self.pf_rows, dtype=i32, device=dev)
+        self.pf_st = torch.zeros(self.pf_rows, dtype=i32, device=dev)
+        self.pf_cpos = torch.zeros(self.pf_rows, dtype=i32, device=dev)
+        self.pf_hl = torch.zeros(max(B, 64), H, dtype=BF16, device=dev)
+
+        self.desc = L.A8Engine(
+            B=B, S=self.S, H=H, ncb=self.ncg, cbk=self.cbk, nsem=self.nsem, vocab=self.emb.shape[0], ras_w=self.ras_w,
+            eos=self.eos, sb=self.sb, do_sample=int(self.do_sample), top_k=self.top_k, top_p=self.top_p,
+            temperature=self.temperature, ras_top_p=self.ras_p, ras_temperature=self.ras_t, seed=self.seed,
+            slow=self.slow.desc, fast=self.fast.desc, emb=L.ptr(self.emb), cbemb=L.ptr(self.cbemb),
+            head=L.ptr(self.head), fast_emb=L.ptr(self.fast_emb), fast_out=L.ptr(self.fast_out), tok=L.ptr(self.tok),
+            hid=L.ptr(self.hid), cpos=L.ptr(self.cpos), prev=L.ptr(self.prev), nstep=L.ptr(self.nstep),
+            tok_in=L.ptr(self.tok_in), frame_prev=L.ptr(self.frame_prev), sil_frame=L.ptr(self.sil_frame),
+            tick_ctr=L.ptr(self.tick_ctr), tick_id=L.ptr(self.tick_id), x_fast2=L.ptr(self.x_fast2),
+            x_fast=L.ptr(self.x_fast), x_slow=L.ptr(self.x_slow), codes=L.ptr(self.codes), logits=L.ptr(self.logits),
+            ld_logits=self.ld_logits, f_pos=L.ptr(self.f_pos), f_pos0=L.ptr(self.f_pos0),
+            f_slot0=L.ptr(self.f_slot0), scratch=self.scratch.desc)
+
+        env_b = os.environ.get("TTS_BATCH_BUCKETS", "").strip()
+        if env_b:
+            buckets = [int(x) for x in env_b.split(",") if x.strip()]
+        if not buckets:
+            buckets = [1, 2, 4, 6, 8, 12, 16, 20, 24, 28, 32, 40, 48, 56, 64, 72, 80, 88, 96, 104, 112, 120, 128,
+                       144, 160, 176, 192]
+        self.buckets = sorted({b for b in buckets if 1 <= b <= B} | {B})
+        self.graphs: Dict[int, torch.cuda.CUDAGraph] = {}
+        self._parts = None
+        self._spk_cache: Dict[str, torch.Tensor] = {}
+        self._pkv: Dict[str, tuple] = {}
+        self.dir = None
+        self.guide = False
+
+    # ------------------------------------------------------------------ the tick
+    def tick(self, b):
+        """One frame for rows [0, b) launched eagerly on the current stream (capture() records it per bucket)."""
+        L.call("a8_tick", C.byref(self.desc), int(b), L.stream_handle())
+
+    def slow_step(self, b):
+        L.call("a8_slow_step", C.byref(self.desc), int(b), L.stream_handle())
+
+    @torch.inference_mode()
+    def capture(self, log=print):
+        """Warm up and record one CUDA graph per bucket (largest first)."""
+        t0 = time.perf_counter()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        order = sorted(self.buckets, reverse=True)
+        with torch.cuda.stream(s):
+            for b in order:
+                for _ in range(2):
+                    self.tick(b)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        for b in order:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.tick(b)
+            self.graphs[b] = g
+        torch.cuda.synchronize()
+        self.reset_state()
+        log(f"[a8] captured {len(self.graphs)} tick graphs {self.buckets} in {time.perf_counter() - t0:.1f}s")
+
+    def reset_state(self):
+        for t in (self.tok, self.cpos, self.hid, self.prev, self.nstep, self.tick_ctr, self.frame_prev):
+            t.zero_()
+
+    def bucket_for(self, n_rows):
+        for b in self.buckets:
+            if b >= n_rows:
+                return b
+        return self.buckets[-1]
+
+    @torch.inference_mode()
+    def replay(self, b, bd=0):
+        self.graphs[b].replay()
+
+    # ---- guidance / director: not on this model (the worker calls these unconditionally) ----
+    def dir_bucket(self):
+        return 0
+
+    def pairs_free(self):
+        return 0
+
+    def clear_groups(self, slots):
+        return None
+
+    def guide_groups(self, groups):
+        if groups:
+            raise NotImplementedError("guided groups (TTS_INSTRUCT_MODE=guide) are not supported by the Audio8 engine")
+
+    def guide_cross(self, entries):
+        return {}
+
+    def attach_director(self, *a, **k):
+        raise NotImplementedError("a guidance director (TTS_GUIDE_DIRECTOR) is not supported by the Audio8 engine")
+
+    # ------------------------------------------------------------------ prompts (serve/fast_engine.py:903-983)
+    def _enc(self, s):
+        return self.tokz.encode(s, add_special_tokens=False)
+
+    def _parts_init(self):
+        e = self._enc
+        self._parts = SimpleNamespace(
+            ref_head=e("<|im_start|>system\n") + e("convert the provided text to speech reference to the following:"
+                                                  "\n\nText:\n"),
+            speech=e("\n\nSpeech:\n"),
+            user=e("<|im_end|>\n") + e("<|im_start|>user\n"),
+            tail=e("<|im_end|>\n") + e("<|im_start|>assistant\n<|voice|>"),
+            noref=e("<|im_start|>system\n") + e("convert the provided text to speech") + e("<|im_end|>\n")
+            + e("<|im_start|>user\n"))
+
+    @staticmethod
+    def _ref_text(text):
+        t = _clean_text(text)
+        return t if re.search(r"<\|speaker:\d+\|>", t) else f"<|speaker:0|>{t}"
+
+    def _prompt_ids(self, item):
+        P = self._parts
+        rc = getattr(item, "ref_code", None) if item is not None else None
+        if rc is None or not getattr(item, "ref_text", ""):
+            ids = torch.tensor(P.noref, dtype=torch.long)
+            return ids, torch.zeros(len(ids), self.ncg, dtype=torch.long), torch.zeros(len(ids), dtype=torch.bool)
+        head = P.ref_head + self._enc(self._ref_text(item.ref_text)) + P.speech
+        codes = rc.long().cpu()
+        T = codes.shape[0]
+        sem = torch.cat([torch.tensor(head, dtype=torch.long), codes[:, 0] + self.sb,
+                         torch.tensor(P.user, dtype=torch.long)])
+        cb = torch.zeros(len(sem), self.ncg, dtype=torch.long)
+        cb[len(head):len(head) + T] = codes
+        aud = torch.zeros(len(sem), dtype=torch.bool)
+        aud[len(head):len(head) + T] = True
+        return sem, cb, aud
+
+    def _prompt_embeds(self, sem, cb, aud):
+        """Slow AR input embeds [L, H]: codebook sum on audio positions only (serve/fast_engine.py:941-945)."""
+        sem, cb, aud = (t.to(self.dev) for t in (sem, cb, aud))
+        e = self.emb[sem]
+        full = (e.float() + self.cbemb[cb + self.cb_off].float().sum(1).to(BF16).float()).to(BF16)
+        return torch.where(aud.unsqueeze(1), full, e)
+
+    def _speaker_prefix(self, key, item):
+        hit = self._spk_cache.get(key)
+        if hit is None:
+            hit = self._prompt_embeds(*self._prompt_ids(item))
+            self._spk_cache[key] = hit
+        return hit
+
+    @torch.inference_mode()
+    def build_prompts(self, reqs):
+        if self._parts is None:
+            self._parts_init()
+        P = self._parts
+        sems, cbs, auds = [], [], []
+        for r in reqs:
+            ctx_t = (r.get("ctx_text") or "").strip()
+            ids = torch.tensor(self._enc(_clean_text((ctx_t + " " if ctx_t else "") + r["text"]) or ".") + P.tail,
+                               dtype=torch.long)
+            cb = torch.zeros(len(ids), self.ncg, dtype=torch.long)
+            aud = torch.zeros(len(ids), dtype=torch.bool)
+            if r.get("ctx_codes") is not None:
+                cc = torch.as_tensor(r["ctx_codes"]).long().reshape(-1, self.ncg)
+                ids = torch.cat([ids, cc[:, 0] + self.sb])
+                cb = torch.cat([cb, cc])
+                aud = torch.cat([aud, torch.ones(len(cc), dtype=torch.bool)])
+            sems.append(ids), cbs.append(cb), auds.append(aud)
+        lens = [len(t) for t in sems]
+        rest_e = torch.split(self._prompt_embeds(torch.cat(sems), torch.cat(cbs), torch.cat(auds)), lens)
+        return [(r["key"], self._speaker_prefix(r["key"], r["item"]), rest_e[i]) for i, r in enumerate(reqs)]
+
+    # ------------------------------------------------------------------ admission (serve/fast_engine.py:1035-1156)
+    def evict_voices(self, keys) -> int:
+        ks, n = set(keys), 0
+        for d in (self._pkv, self._spk_cache):
+            for k in [k for k in d if k in ks]:
+                del d[k]
+                n += 1
+        return n
+
+    def voice_state_bytes(self) -> int:
+        n = sum(t.numel() * t.element_size() for kv in self._pkv.values() for t in kv)
+        return n + sum(t.numel() * t.element_size() for t in self._spk_cache.values())
+
+    def prime_speaker(self, key, item):
+        self.prime_speakers([(key, item)])
+
+    def prime_speakers(self, pairs):
+        """TTS_VOC_PRIME=0 (the reference's default): rows start with a clean codec state, nothing to prime."""
+        return None
+
+    def _forward_rows(self, x, pos, slot, max_len):
+        """Packed causal prefill of rows x [n, H] (bf16, consumed) at positions pos into cache rows slot."""
+        n = x.shape[0]
+        assert n <= self.pf_rows
+        self.pf_pos[:n].copy_(pos, non_blocking=True)
+        self.pf_slot[:n].copy_(slot, non_blocking=True)
+        run = L.A8StackRun(x=L.ptr(x), ldx=self.H, rows=n, pos=L.ptr(self.pf_pos), slot=L.ptr(self.pf_slot),
+                           lens=None, lens_max=0, rowmap=L.ptr(self.pf_slot), max_len=int(max_len),
+                           scratch=self.scratch.desc)
+        L.call("a8_stack_forward", C.byref(self.slow.desc), C.byref(run), L.stream_handle())
+        return self.scratch.h[:n]
+
+    def _prefix_kv(self, pkey, prefix):
+        """A voice prefix's K/V for every slow layer, computed once into the scratch row and kept (:1073-1087)."""
+        hit = self._pkv.get(pkey)
+        if hit is not None:
+            return hit
+        Lp = prefix.shape[0]
+        pos = torch.arange(Lp, dtype=torch.int32, device=self.dev)
+        slot = torch.full((Lp,), self.SCR, dtype=torch.int32, device=self.dev)
+        for a in range(0, Lp, self.pf_rows):
+            e = min(Lp, a + self.pf_rows)
+            self._forward_rows(prefix[a:e].clone(), pos[a:e], slot[a:e], e)
+        kv = (self.slow.kc[:, self.SCR, :, :Lp].clone(), self.slow.vc[:, self.SCR, :, :Lp].clone())
+        self._pkv[pkey] = kv
+        return kv
+
+    @torch.inference_mode()
+    def admit(self, slots: List[int], reqs: List[dict]):
+        """Packed prefill of reqs into free slots. Returns each prompt's length, or -1 for one that can't fit."""
+        parts = self.build_prompts(reqs)
+        lens = [(p.shape[0] if p is not None else 0) + r.shape[0] for _, p, r in parts]
+        limit = min(self.S - 32, self.prefill_tokens)
+        ok = [i for i, n in enumerate(lens) if n <= limit]
+        cap = min(self.prefill_tokens, self.pf_rows)
+        chunk, tot = [], 0
+        for i in ok:
+            n = parts[i][2].shape[0]
+            if chunk and (tot + n > cap or len(chunk) >= self.B):
+                self._prefill([slots[k] for k in chunk], [reqs[k] for k in chunk], [parts[k] for k in chunk])
+                chunk, tot = [], 0
+            chunk.append(i)
+            tot += n
+        if chunk:
+            self._prefill([slots[k] for k in chunk], [reqs[k] for k in chunk], [parts[k] for k in chunk])
+        return [n if n <= limit else -1 for n in lens]
+
+    def _prefill(self, slots, reqs, parts):
+        dev = self.dev
+        p0 = {}
+        groups: Dict[str, List[int]] = {}
+        for s, (pkey, prefix, _) in zip(slots, parts):
+            if pkey is not None:
+                groups.setdefault(pkey, []).append(s)
+        for pkey, gslots in groups.items():
+            prefix = next(p for (k, p, _) in parts if k == pkey)
+            k, v = self._prefix_kv(pkey, prefix)
+            Lp = prefix.shape[0]
+            idx = torch.tensor(gslots, dtype=torch.long, device=dev)
+            self.slow.kc[:, idx, :, :Lp] = k.unsqueeze(1)
+            self.slow.vc[:, idx, :, :Lp] = v.unsqueeze(1)
+            for s in gslots:
+                p0[s] = Lp
+        rests = [r for _, _, r in parts]
+        ns = [int(r.shape[0]) for r in rests]
+        starts = [p0.get(s, 0) for s in slots]
+        x = torch.cat(rests, 0).contiguous()
+        pos = torch.cat([torch.arange(a, a + n, dtype=torch.int32) for a, n in zip(starts, ns)]).to(dev)
+        slot_t = torch.cat([torch.full((n,), s, dtype=torch.int32) for n, s in zip(ns, slots)]).to(dev)
+        max_len = max(a + n for a, n in zip(starts, ns))
+        h = self._forward_rows(x, pos, slot_t, max_len)
+        last = torch.tensor(np.cumsum(ns) - 1, dtype=torch.int32, device=dev)
+        k = len(slots)
+        self.pf_last[:k].copy_(last)
+        L.call("a8_gather_rows", L.ptr(h), self.H, L.ptr(self.pf_last), L.ptr(self.pf_hl), self.H, k, self.H,
+               L.stream_handle())
+        self.pf_st[:k].copy_(torch.tensor(slots, dtype=torch.int32))
+        self.pf_cpos[:k].copy_(torch.tensor([a + n for a, n in zip(starts, ns)], dtype=torch.int32))
+        L.call("a8_prefill_finish", C.byref(self.desc), L.ptr(self.pf_hl), k, L.ptr(self.pf_st), L.ptr(self.pf_cpos),
+               L.stream_handle())
+        # codec rows: keep_voc rows keep their state; the others start clean; both decode a silence frame first
+        idx = torch.tensor(slots, dtype=torch.long, device=dev)
+        self.frame_prev.index_copy_(0, idx, self.sil_frame.unsqueeze(0).expand(len(slots), -1).contiguous())
+        fresh = [s for s, r in zip(slots, reqs) if not r.get("keep_voc")]
+        if fresh and self.voc is not None:
+            self.voc.clear_many(fresh)

@@ -1,0 +1,226 @@
+/* audio8_b200.h -- C ABI of the B200 (sm_100a) Audio8 decode-tick library, libaudio8_b200.so.
+ *
+ * Plain pointers (device memory unless stated), sizes and a CUDA stream; every function returns 0 (A8_OK) or an
+ * A8_ERR_* code and never throws. All launches are asynchronous on the given stream and capture-safe (no host
+ * synchronisation, no allocation), so a caller may record them into a CUDA graph.
+ *
+ * Each entry point replaces a piece of the reference engine (serve/fast_kernels.py, serve/fast_engine.py of
+ * lvt1693/audio8-turbo-engine); the comment above it names the reference interface (file:line).
+ *
+ * Device-side waits are bounded: a wait that runs out records an error code readable with a8_get_error() and the
+ * kernel returns; a8_get_error() is the only call here that synchronises with the device.
+ */
+#ifndef AUDIO8_B200_H
+#define AUDIO8_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* a8_stream_t; /* a cudaStream_t */
+
+enum {
+  A8_OK = 0,
+  A8_ERR_ARG = 1,    /* bad argument (null pointer, unsupported shape) */
+  A8_ERR_CUDA = 2,   /* a CUDA runtime / driver call failed */
+  A8_ERR_ALIGN = 3,  /* a pointer or stride breaks a 16-byte TMA alignment rule */
+  A8_ERR_SIZE = 4,   /* a workspace or a table is too small for the request */
+  A8_ERR_DEVICE = 5  /* no sm_100 device current */
+};
+
+/* ---------------------------------------------------------------------------------------------- status */
+/* 1 when the current device is a compute-capability 10.0 GPU (B200), else 0. */
+int a8_device_ok(void);
+/* Device error record of the bounded waits: out[0] code (0 = none), out[1] kernel id, out[2] block, out[3] extra.
+ * Synchronises the device. */
+int a8_get_error(int out[4]);
+int a8_clear_error(void);
+
+/* ---------------------------------------------------------------------------------------------- GEMM */
+/* Epilogue kinds of a8_gemm. Y = X[M,K] . W[N,K]^T accumulated in fp32 on the tensor cores (tcgen05, TMEM). */
+enum {
+  A8_EPI_BF16 = 0,      /* y bf16 [M, ldy]:   bf16(acc (+ bias))                                           */
+  A8_EPI_F32_ROUND = 1, /* y fp32 [M, ldy]:   float(bf16(acc)) -- the reference's bf16 logits as fp32      */
+  A8_EPI_SILU = 2,      /* W rows interleaved per 64 (gate 0-63, up 64-127 of every 128): y bf16 [M, N/2]:
+                           bf16(bf16(silu(bf16 g)) * bf16 u)                                               */
+  A8_EPI_ROPE = 3,      /* fused qkv epilogue: bias, RoPE (rotate_half, fp32, one rounding), q -> y [M, nq, hd],
+                           k / v -> caches at [slot, head, pos % ring]                                      */
+  A8_EPI_GELU = 4,      /* y bf16: bf16(gelu_erf(bf16(acc + bias)))                                        */
+  A8_EPI_LSRES = 5      /* y bf16: bf16(res + bf16(gamma * bf16(acc + bias)))  (ConvNeXt layer scale)      */
+};
+
+typedef struct A8Epilogue {
+  int kind;
+  const void* bias;  /* bf16 [N] or NULL */
+  /* A8_EPI_ROPE */
+  const void* cos;   /* bf16 [npos, hd] rotate_half table (cos of both halves) */
+  const void* sin;   /* bf16 [npos, hd] */
+  const int* pos;    /* int32 [M] rope position of each token row */
+  const int* slot;   /* int32 [M] cache row of each token row */
+  void* kc;          /* bf16 [rows, nkv, cache_len, hd] */
+  void* vc;
+  int nq, nkv, hd, ring, cache_len;
+  /* A8_EPI_LSRES */
+  const void* gamma; /* bf16 [N] */
+  const void* res;   /* bf16 [M, ldres] (may equal y) */
+  int ldres;
+} A8Epilogue;
+
+/* Workspace of a8_gemm for a shape (splits 0 = automatic). ws_floats / n_counters may be 0 (no split-K). */
+int a8_gemm_workspace(int N, int K, int M, int splits, long long* ws_floats, int* n_counters);
+
+/* y = epilogue(x[M, K] . w[N, K]^T). x row stride ldx, w dense; bf16. Replaces GemmDispatch / linear_triton
+ * (serve/fast_kernels.py:364-520) and, through the epilogues, bias_rope_store (:139-187) and silu_mul (:526-545).
+ * ws / counters: split-K scratch from a8_gemm_workspace (counters zeroed once before first use). */
+int a8_gemm(const void* x, int ldx, const void* w, int N, int K, int M, void* y, int ldy, const A8Epilogue* epi,
+            float* ws, long long ws_floats, int* counters, int n_counters, int splits, a8_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------- attention */
+/* Workspace of a8_attention / a8_stack_forward's attention for `rows` query rows whose key count is at most max_len. */
+int a8_attention_workspace(int rows, int nkv, int hd, int max_len, long long* ws_floats, int* n_counters);
+
+/* out[r, h, :] = softmax(q[r, h] . K[c, h / group, :L_r] * scale) V[c, h / group, :L_r], c = rowmap[r] (or r),
+ * L_r = min(lens[r], max_len); caches bf16 [layers, cache_rows, nkv, cache_len, hd], hd 64 or 128.
+ * Replaces DecodeAttention (serve/fast_kernels.py:193-290) and, with lens = pos + 1 and rowmap = the request's
+ * slot, prefill_attention (:296-358). scale <= 0: hd^-0.5. */
+int a8_attention(const void* q, int q_stride, const void* kc, const void* vc, int layers, int cache_rows, int nq,
+                 int nkv, int hd, int cache_len, int layer, const int* lens, const int* rowmap, int rows, int max_len,
+                 float scale, void* out, int out_stride, float* ws, long long ws_floats, int* counters, int n_counters,
+                 a8_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------- row kernels */
+/* y = bf16(w * bf16(h * rsqrt(mean(h^2) + eps))), h = bf16(x + res) stored back into res (res may be NULL: h = x).
+ * N <= 1024, a multiple of 8. Replaces rmsnorm (serve/fast_kernels.py:30-69). */
+int a8_rmsnorm(const void* x, int ldx, void* res, int ldr, const void* w, void* y, int ldy, int rows, int N, float eps,
+               a8_stream_t stream);
+/* x[r] = emb[sem[r]] + bf16(sum_k cbemb[codes[r, k] + cbk k]) (serve/fast_engine.py:715-717). */
+int a8_embed_frame(const int64_t* sem, const int64_t* codes, int ncb, int cbk, const void* emb, const void* cbemb,
+                   void* x, int ldx, int rows, int H, int vocab, a8_stream_t stream);
+/* Tick start (serve/fast_engine.py:742-749, :705): tok_in = tok, codes[:, 0] = clamp(tok - sb), fast AR rows
+ * x2[2r] = hid[r], x2[2r+1] = fast_emb[codes[r, 0]]; tick_id[0] = ctr[0]++ (ctr may be NULL). */
+int a8_tick_start(const int64_t* tok, int64_t* tok_in, int64_t* codes, int ncb, long long sb, int cbk, const void* hid,
+                  const void* fast_emb, void* x2, int rows, int H, long long* ctr, long long* tick_id,
+                  a8_stream_t stream);
+/* y[r] = src[idx[r]] (bf16 rows of H). */
+int a8_gather_rows(const void* src, int lds, const int* idx, void* y, int ldy, int rows, int H, a8_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------- sampling */
+/* out[r] = draw over logits[r, :V] (fp32): top-k (ties: lower index first), top-p on the untempered softmax (the best
+ * candidate always kept), temperature, exponential race with E = -log(u), u from Philox4x32-10(key = seed,
+ * counter = (i / 4, r, tick_id[0] (0 if NULL), stream_id)); do_sample = 0: argmax (first index).
+ * Replaces _Sampler (serve/fast_engine.py:141-172). */
+int a8_sample(const float* logits, int ld, int V, int rows, int do_sample, int top_k, float top_p, float temperature,
+              unsigned long long seed, int stream_id, const long long* tick_id, int64_t* out, a8_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------- stacks */
+typedef struct A8Scratch {
+  void* h;              /* bf16 [rows, dim]: normed activations; after a stack forward, its final-normed output */
+  void* q;              /* bf16 [rows, nq * hd] */
+  void* o;              /* bf16 [rows, nq * hd] */
+  void* a;              /* bf16 [rows, dim] */
+  void* mlp;            /* bf16 [rows, inter] */
+  float* ws;            /* GEMM split-K partials (a8_gemm_workspace) */
+  long long ws_floats;
+  int* counters;        /* zeroed once */
+  int n_counters;
+  float* attn_ws;       /* attention split partials (a8_attention_workspace) */
+  long long attn_ws_floats;
+  int* attn_counters;   /* zeroed once */
+  int n_attn_counters;
+} A8Scratch;
+
+/* A transformer stack on packed weights (serve/fast_engine.py:82-115): q / k rows of wqkv permuted per head for
+ * rotate_half, w13 = gate and up rows interleaved per 64 (rows 128t..128t+63 = w1[64t..], +64..+127 = w3[64t..]),
+ * LayerScale folded into wo / w2 where the model has one. */
+typedef struct A8StackDesc {
+  int layers, dim, nq, nkv, hd, inter;
+  float eps;
+  const void* wqkv;     /* bf16 [layers, (nq + 2 nkv) hd, dim] */
+  const void* bqkv;     /* bf16 [layers, (nq + 2 nkv) hd] or NULL */
+  const void* wo;       /* bf16 [layers, dim, nq hd] */
+  const void* w13;      /* bf16 [layers, 2 inter, dim] */
+  const void* w2;       /* bf16 [layers, dim, inter] */
+  const void* ln1;      /* bf16 [layers, dim] */
+  const void* ln2;      /* bf16 [layers, dim] */
+  const void* norm;     /* bf16 [dim] */
+  const void* cos;      /* bf16 [npos, hd] */
+  const void* sin;      /* bf16 [npos, hd] */
+  void* kc;             /* bf16 [layers, cache_rows, nkv, cache_len, hd] */
+  void* vc;
+  int cache_rows, cache_len, ring;   /* ring 0: positions stored at pos, else at pos % ring */
+} A8StackDesc;
+
+typedef struct A8StackRun {
+  void* x;              /* bf16 [rows, ldx] input rows, consumed as the residual stream (updated in place) */
+  int ldx;
+  int rows;
+  const int* pos;       /* int32 [rows] RoPE position */
+  const int* slot;      /* int32 [rows] cache row the K/V go to (NULL: the row index) */
+  const int* lens;      /* int32 [rows] keys attended (NULL: pos + 1) */
+  int lens_max;         /* clamp of the keys attended (0: cache_len) */
+  const int* rowmap;    /* int32 [rows] cache row attended (NULL: the row index) */
+  int max_len;          /* bound of any row's keys (0: cache_len); sets the split count */
+  A8Scratch scratch;    /* output in scratch.h */
+} A8StackRun;
+
+/* _Stack.forward (serve/fast_engine.py:117-138): decode rows or packed causal prefill rows. */
+int a8_stack_forward(const A8StackDesc* d, const A8StackRun* r, a8_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------- engine */
+typedef struct A8Engine {
+  int B, S, H, ncb, cbk, nsem, vocab, ras_w;
+  long long eos, sb;
+  int do_sample, top_k;
+  float top_p, temperature, ras_top_p, ras_temperature;
+  unsigned long long seed;
+  A8StackDesc slow, fast;
+  const void* emb;        /* bf16 [vocab, H] */
+  const void* cbemb;      /* bf16 [ncb cbk, H] */
+  const void* head;       /* bf16 [nsem + 1, H]: semantic rows then EOS */
+  const void* fast_emb;   /* bf16 [cbk, H] */
+  const void* fast_out;   /* bf16 [cbk, H] */
+  /* slot state (fixed addresses; rows >= B are scratch) */
+  int64_t* tok;           /* [B + 1] */
+  void* hid;              /* bf16 [B + 1, H] */
+  int* cpos;              /* [B + 1] */
+  int64_t* prev;          /* [B + 1, ras_w] */
+  int* nstep;             /* [B + 1] */
+  int64_t* tok_in;        /* [B] */
+  int64_t* frame_prev;    /* [B, ncb] */
+  const int64_t* sil_frame; /* [ncb] */
+  long long* tick_ctr;    /* [1] ticks run so far (the sampling noise's tick counter) */
+  long long* tick_id;     /* [1] */
+  /* tick scratch */
+  void* x_fast2;          /* bf16 [2B, H] */
+  void* x_fast;           /* bf16 [B, H] */
+  void* x_slow;           /* bf16 [B, H] */
+  int64_t* codes;         /* [B, ncb] */
+  float* logits;          /* [B, ld_logits] */
+  int ld_logits;
+  const int* f_pos;       /* int32 [ncb, 2B]: row i all equal to i */
+  const int* f_pos0;      /* int32 [2B]: r % 2 */
+  const int* f_slot0;     /* int32 [2B]: r / 2 */
+  A8Scratch scratch;      /* for 2B rows */
+} A8Engine;
+
+/* One frame for slot rows [0, b): fast AR (2-token pass + ncb - 2 passes, each sampled), slow AR step, semantic
+ * draw with RAS, state update. Replaces FastEngine._tick (serve/fast_engine.py:737-769) minus the codec. */
+int a8_tick(const A8Engine* e, int b, a8_stream_t stream);
+
+/* The slow AR half of the tick for rows [0, b), reading tok_in and codes as left by the tick's first half: input
+ * embedding, 24-layer step at positions cpos, semantic head, draw with RAS, state update
+ * (serve/fast_engine.py:750-769). */
+int a8_slow_step(const A8Engine* e, int b, a8_stream_t stream);
+
+/* Admission tail for n requests (serve/fast_engine.py:1124-1133 and _pf_body :828-835): h_last bf16 [n, H] = each
+ * request's final-normed last prompt row; first token drawn without the RAS window (noise stream 18 at the current
+ * tick count), written with hid, cpos = cpos_new into slots[i]; prev and nstep of those slots cleared. */
+int a8_prefill_finish(const A8Engine* e, const void* h_last, int n, const int* slots, const int* cpos_new,
+                      a8_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AUDIO8_B200_H */
