@@ -71,11 +71,11 @@ def test_gemm_bias_gelu_lsres_f32(L, ws):
     acc = x.float() @ w.float().t()
     # bias
     y = torch.zeros(M, N, dtype=BF, device="cuda")
-    gemm(L, ws, x.cuda(), w.cuda(), y, L.A8Epilogue(kind=L.EPI_BF16, bias=L.ptr(b.cuda())))
+    bc = b.cuda()
+    gemm(L, ws, x.cuda(), w.cuda(), y, L.A8Epilogue(kind=L.EPI_BF16, bias=L.ptr(bc)))
     ref = R.bf(acc + b.float())
     assert rel(y, ref) < 1e-2 and frac_equal(y, ref) > 0.97
     # gelu(bf16(acc + b)) (ConvNeXt pwconv1)
-    bc = b.cuda()
     gemm(L, ws, x.cuda(), w.cuda(), y, L.A8Epilogue(kind=L.EPI_GELU, bias=L.ptr(bc)))
     ref = R.bf(torch.nn.functional.gelu(R.bf(acc + b.float())))
     assert rel(y, ref) < 1e-2 and frac_equal(y, ref) > 0.97
@@ -119,11 +119,13 @@ def test_gemm_rope_store(L, ws, shape):
     N = (nq + 2 * nkv) * hd
     x, w = rnd(g, M, D), rnd(g, N, D, scale=D ** -0.5)
     b = rnd(g, N, scale=0.3) if has_b else None
-    npos = 700
+    npos = 700 if ring < clen * 2 else clen
     cos, sin = R.rope_tables(base, hd, npos)
-    pos = torch.randint(0, npos, (M,), generator=g, dtype=torch.int32)
+    # distinct cache cells (two tokens writing one cell would make the stored value depend on write order)
+    col = torch.randperm(min(clen, ring), generator=g)[:M]
+    pos = (col + min(clen, ring) * torch.randint(0, npos // min(clen, ring), (M,), generator=g)).to(torch.int32)
     slot = torch.randint(0, rows, (M,), generator=g, dtype=torch.int32)
-    slot[1], pos[1] = slot[0], (pos[0] + 1) % npos
+    slot[1] = slot[0]
     kc_o = torch.zeros(rows, nkv, clen, hd)
     vc_o = torch.zeros_like(kc_o)
     q_o = R.bias_rope_store(R.linear(x.float(), w.float()), b.float() if b is not None else None, cos, sin, pos, slot,
@@ -225,8 +227,9 @@ def test_embed_frame(L):
     sem = torch.randint(0, V, (b,), generator=g)
     codes = torch.randint(0, cbk, (b, ncb), generator=g)
     x = torch.zeros(b, H, dtype=BF, device="cuda")
-    L.call("a8_embed_frame", L.ptr(sem.cuda()), L.ptr(codes.cuda()), ncb, cbk, L.ptr(emb.cuda()), L.ptr(cbemb.cuda()),
-           L.ptr(x), H, b, H, V, L.stream_handle())
+    d = [t.cuda() for t in (sem, codes, emb, cbemb)]        # kept alive until the kernel has run
+    L.call("a8_embed_frame", L.ptr(d[0]), L.ptr(d[1]), ncb, cbk, L.ptr(d[2]), L.ptr(d[3]), L.ptr(x), H, b, H, V,
+           L.stream_handle())
     torch.cuda.synchronize()
     off = (torch.arange(ncb) * cbk).view(1, -1)
     ref = R.bf(emb.float()[sem] + R.bf(cbemb.float()[codes + off].sum(1)))
@@ -242,13 +245,14 @@ def test_sampler_exact(L, V, k, p, t):
     lg[3, 100:110] = lg[3].max()                                   # a tie group at the top
     out = torch.empty(rows, dtype=torch.int64, device="cuda")
     tick = torch.tensor([5], dtype=torch.int64, device="cuda")
-    L.call("a8_sample", L.ptr(lg.cuda()), V, V, rows, 1, k, p, t, 1234, 17, L.ptr(tick), L.ptr(out),
+    LG = lg.cuda()
+    L.call("a8_sample", L.ptr(LG), V, V, rows, 1, k, p, t, 1234, 17, L.ptr(tick), L.ptr(out),
            L.stream_handle())
     torch.cuda.synchronize()
     kk = k if 0 < k < V else V
     v, idx, cum = R.topk_filter(lg, kk)
     ref = R.draw(v, idx, cum, p, t, R.philox_exp(1234, 17, 5, list(range(rows)), kk))
     assert torch.equal(out.cpu(), ref)
-    L.call("a8_sample", L.ptr(lg.cuda()), V, V, rows, 0, k, p, t, 0, 0, None, L.ptr(out), L.stream_handle())
+    L.call("a8_sample", L.ptr(LG), V, V, rows, 0, k, p, t, 0, 0, None, L.ptr(out), L.stream_handle())
     torch.cuda.synchronize()
     assert torch.equal(out.cpu(), lg.argmax(-1))
