@@ -27,7 +27,6 @@ class A8Epilogue(C.Structure):
 
 class A8Scratch(C.Structure):
     _fields_ = [("h", c_void_p), ("q", c_void_p), ("o", c_void_p), ("a", c_void_p), ("mlp", c_void_p),
-                ("ws", c_void_p), ("ws_floats", c_ll), ("counters", c_void_p), ("n_counters", c_int),
                 ("attn_ws", c_void_p), ("attn_ws_floats", c_ll), ("attn_counters", c_void_p),
                 ("n_attn_counters", c_int)]
 
@@ -65,9 +64,9 @@ SIGNATURES = {
     "a8_device_ok": (c_int, []),
     "a8_get_error": (c_int, [C.POINTER(c_int)]),
     "a8_clear_error": (c_int, []),
-    "a8_gemm_workspace": (c_int, [c_int, c_int, c_int, c_int, C.POINTER(c_ll), C.POINTER(c_int)]),
+    "a8_launch_count": (c_ll, []),
     "a8_gemm": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_void_p, c_int, C.POINTER(A8Epilogue),
-                        c_void_p, c_ll, c_void_p, c_int, c_int, c_void_p]),
+                        c_int, c_void_p]),
     "a8_attention_workspace": (c_int, [c_int, c_int, c_int, c_int, C.POINTER(c_ll), C.POINTER(c_int)]),
     "a8_attention": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                              c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_int, c_void_p, c_ll, c_void_p,

@@ -305,6 +305,7 @@ static int launch_attn(const CUtensorMap& mk, const CUtensorMap& mv, const AttnA
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
+  ++g_launches;
   return cudaLaunchKernelEx(&cfg, k_attn<HD, GROUP, CHUNK>, mk, mv, a) == cudaSuccess ? A8_OK : A8_ERR_CUDA;
 }
 

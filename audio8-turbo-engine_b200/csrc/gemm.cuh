@@ -13,11 +13,9 @@ struct GemmArgs {
   int ldy;              // output row stride (elements)
   int ntok;             // token tile = UMMA N (multiple of 16, <= 256)
   int n_tiles, tok_tiles;
-  int kb_total, kb_per_split, splits;
+  int kb_total, kb_per_split, splits;   // splits > 1: the K splits of a tile are one cluster (blockIdx.z = rank)
   int stages;
   uint32_t tmem_cols;
-  float* ws;            // split-K partials [splits][tiles][ntok32][128]
-  int* counters;        // [tiles], zero between launches (the reducing block resets its entry)
   void* y;
   A8Epilogue epi;
 };
@@ -33,7 +31,7 @@ struct GemmPlan {
 
 // Builds the tensor maps and launch shape. Returns 0 or an A8_ERR_* code.
 int gemm_plan(GemmPlan* p, const void* x, int ldx, const void* w, int N, int K, int M, void* y, int ldy,
-              const A8Epilogue* epi, float* ws, long long ws_floats, int* counters, int n_counters, int splits);
+              const A8Epilogue* epi, int splits);
 int gemm_launch(const GemmPlan* p, cudaStream_t s, bool pdl);
 
 int encode_map_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,

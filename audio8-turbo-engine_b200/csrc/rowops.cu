@@ -152,6 +152,7 @@ static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, void** args
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
+  ++g_launches;
   return cudaLaunchKernelExC(&cfg, fn, args);
 }
 

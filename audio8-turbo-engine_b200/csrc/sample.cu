@@ -389,6 +389,7 @@ int sample_launch(const SampleArgs& a, int rows, cudaStream_t s) {
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
+  ++g_launches;
   return cudaLaunchKernelEx(&cfg, k_sample, a) == cudaSuccess ? A8_OK : A8_ERR_CUDA;
 }
 

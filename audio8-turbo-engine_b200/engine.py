@@ -100,20 +100,18 @@ class PackedStack:
 
 
 class Scratch:
-    """Activation and split-K buffers for up to `rows` token rows of stacks up to `dim` / `inter` wide."""
+    """Activation buffers and the attention's split workspace for up to `rows` token rows of stacks up to `dim` /
+    `inter` wide."""
 
-    def __init__(self, rows, dim, qdim, inter, nkv, hd, max_len, dev, gemm_floats=1 << 24, counters=8192):
+    def __init__(self, rows, dim, qdim, inter, nkv, hd, max_len, dev):
         mk = lambda n: torch.zeros(rows, n, dtype=BF16, device=dev)
         self.h, self.q, self.o, self.a, self.mlp = mk(dim), mk(qdim), mk(qdim), mk(dim), mk(inter)
-        self.ws = torch.zeros(gemm_floats, dtype=torch.float32, device=dev)
-        self.counters = torch.zeros(counters, dtype=torch.int32, device=dev)
         n = C.c_longlong()
         L.check(L.load().a8_attention_workspace(rows, nkv, hd, max_len, C.byref(n), None), "attention workspace")
         self.attn_ws = torch.zeros(max(1, n.value), dtype=torch.float32, device=dev)
         self.attn_counters = torch.zeros(rows * nkv, dtype=torch.int32, device=dev)
         self.desc = L.A8Scratch(
-            h=L.ptr(self.h), q=L.ptr(self.q), o=L.ptr(self.o), a=L.ptr(self.a), mlp=L.ptr(self.mlp), ws=L.ptr(self.ws),
-            ws_floats=self.ws.numel(), counters=L.ptr(self.counters), n_counters=self.counters.numel(),
+            h=L.ptr(self.h), q=L.ptr(self.q), o=L.ptr(self.o), a=L.ptr(self.a), mlp=L.ptr(self.mlp),
             attn_ws=L.ptr(self.attn_ws), attn_ws_floats=self.attn_ws.numel(), attn_counters=L.ptr(self.attn_counters),
             n_attn_counters=self.attn_counters.numel())
 

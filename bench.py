@@ -1,0 +1,373 @@
+#!/usr/bin/env python3
+"""Benchmark of the Audio8 decode tick on B200 (one JSON line on stdout, rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg1]
+
+Workload cfg1: the slow-AR decode step alone, bf16, bucket of 64 slots, each slot's KV
+length drawn uniform in [200, 1500] from seed 1, one new token a slot, the stand-in model's full shapes (24 layers,
+896 wide, GQA 14/2, FFN 4864, semantic head of 4097 rows). A step = input embedding + 24 layers + head + semantic draw
++ state update, replayed from one CUDA graph; every slot's position is restored before each step so the workload is
+the same at every step. Data: synthetic (seeded random weights and KV; no checkpoint or dataset is involved).
+
+--impl reference times the reference's own CPU implementation of the path: the reference has none (Triton only),
+so it is the CPU restatement oracle/ref_cpu.py on all host threads, on a bounded sample of the same workload.
+Multi-GPU (torchrun, N > 1): one independent replica per GPU (streams shard across replicas; nothing is exchanged),
+value = all ranks' frames / the slowest rank's time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+B_CFG1 = 64
+L_LO, L_HI = 200, 1500
+METRIC = "tick frames/s"
+UNIT = "frames/s"
+
+
+def _peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples (SM clock, throttle reasons) while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.t.join(timeout=2)
+
+    def summary(self):
+        rows = [r for r in self.rows if len(r) >= 9]
+        if not rows:
+            return None
+        sm = sorted(float(r[1]) for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows)}
+
+
+def cfg1_lengths():
+    import torch
+    g = torch.Generator().manual_seed(1)
+    return torch.randint(L_LO, L_HI + 1, (B_CFG1,), generator=g)
+
+
+def cfg1_bytes_flops(lens, layers=24):
+    """Algorithmic HBM bytes and FLOPs of one cfg1 step (no padding rows or columns counted)."""
+    b = len(lens)
+    sl = int(lens.sum())
+    w_layer = (1152 * 896 + 1152) * 2 + 896 * 896 * 2 + 9728 * 896 * 2 + 896 * 4864 * 2 + 2 * 896 * 2
+    weights = layers * w_layer + 4097 * 896 * 2
+    kv = layers * 2 * 2 * 64 * 2 * sl                       # K and V, 2 kv heads, hd 64, bf16
+    kv_write = layers * 2 * 2 * 64 * 2 * b
+    flops = 2 * b * (layers * 14_909_440 + 4097 * 896) + layers * 4 * 14 * 64 * sl
+    return weights + kv + kv_write, flops, kv // layers
+
+
+def cpu_sample(steps, threads=None):
+    """The CPU restatement of the cfg1 step (all host threads): frames/s over a bounded number of steps."""
+    import torch
+    from oracle import ref_cpu as R
+    from oracle.standin import StandinConfig, build_standin
+    torch.set_num_threads(threads or os.cpu_count())
+    m = build_standin(0, StandinConfig(fast_n_layer=1, codec_n_layer=1))
+    c = m.config
+    lens = cfg1_lengths()
+    st = R.Stack(m.layers, m.norm, c.n_head, c.n_local_heads, c.head_dim, c.norm_eps, c.rope_base,
+                 cache_rows=B_CFG1 + 1, cache_len=int(lens.max()) + 1, max_pos=int(lens.max()) + 1)
+    g = torch.Generator().manual_seed(3)
+    st.kc.copy_(R.bf(torch.randn(st.kc.shape, generator=g)))
+    st.vc.copy_(R.bf(torch.randn(st.vc.shape, generator=g)))
+    emb = R.bf(m.embeddings.weight.detach().float())
+    head = torch.cat([emb[c.semantic_begin_id:c.semantic_end_id + 1], emb[c.eos_token_id:c.eos_token_id + 1]])
+    x = R.bf(torch.randn(B_CFG1, c.dim, generator=g) * 0.1)
+    pos = (lens - 1).to(torch.int32)
+    ar = torch.arange(B_CFG1, dtype=torch.int32)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        h = st.forward(x.clone(), pos, ar, pos + 1, rowmap=False)
+        R.linear(h, head).argmax(-1)
+    dt = time.perf_counter() - t0
+    return B_CFG1 * steps / dt, torch.get_num_threads(), dt
+
+
+def run_reference(args):
+    value, cores, dt = cpu_sample(max(1, args.steps))
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": 0, "ms_per_step": round(1000 * dt / max(1, args.steps), 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 rounding points)",
+            "data": "synthetic", "config": cfg_dict(1),
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": f"{args.steps} cfg1 steps (64 rows, KV U[200,1500], 24 layers + head)"},
+            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def cfg_dict(world):
+    return {"workload": "cfg1: slow-AR decode step, bf16, 64 slots, KV length U[200,1500] (seed 1), 1 token a slot",
+            "model": "Audio8 stand-in (seeded random weights, reference shapes)", "global_batch": B_CFG1 * world,
+            "seq_len": f"{L_LO}-{L_HI}", "parallelism": f"replicas x{world}",
+            "l2": "inputs larger than L2 (716 MB weights + ~670 MB KV a step)"}
+
+
+def run_ours(args, rank, world, local):
+    import ctypes as C
+
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__ as G
+    from oracle.standin import StandinConfig, StubTokenizer, build_standin
+    G.build()
+    a8 = G.load_package()
+    L = a8._lib
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    model = build_standin(0, StandinConfig(codec_n_layer=1))
+    gp = dict(do_sample=True, temperature=0.8, top_k=50, top_p=0.95)
+    eng = a8.FastEngine(model, StubTokenizer(), gp, max_slots=B_CFG1, max_seq=2048, buckets=[B_CFG1],
+                        seq_from_env=False, seed=1234 + rank)
+    del model
+    b = B_CFG1
+    lens = cfg1_lengths()
+    g = torch.Generator(device=dev).manual_seed(3 + rank)
+    for t in (eng.slow.kc, eng.slow.vc):
+        t[:, :b].normal_(generator=g)
+    cpos0 = (lens - 1).to(torch.int32).to(dev)
+    eng.cpos[:b].copy_(cpos0)
+    tok0 = (eng.sb + torch.randint(0, 4096, (b,), generator=g, device=dev)).long()
+    codes0 = torch.randint(0, 4096, (b, eng.ncg), generator=g, device=dev)
+    eng.tok_in.copy_(tok0)
+    eng.codes.copy_(codes0)
+    eng.hid[:b].normal_(generator=g)
+    eng.nstep[:b].fill_(5)
+
+    def step():
+        eng.cpos[:b].copy_(cpos0)
+        eng.slow_step(b)
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    n0 = L.load().a8_launch_count()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    launches = L.load().a8_launch_count() - n0
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.barrier()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t)
+    value = world * b * args.steps / (ms / 1000.0)
+    err = a8.device_error()
+    assert err[0] == 0, err
+
+    # end to end through the public API: the step's inputs from pinned host memory, the drawn tokens back
+    h_tok = tok0.cpu().pin_memory()
+    h_codes = codes0.cpu().pin_memory()
+    h_out = torch.empty(b, dtype=torch.int64).pin_memory()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record()
+    for _ in range(args.steps):
+        eng.tok_in.copy_(h_tok, non_blocking=True)
+        eng.codes.copy_(h_codes, non_blocking=True)
+        graph.replay()
+        h_out.copy_(eng.tok[:b], non_blocking=True)
+    e3.record()
+    torch.cuda.synchronize()
+    ms_e2e = e2.elapsed_time(e3)
+    t = torch.tensor([ms_e2e], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_e2e = float(t)
+    e2e = {"value": round(world * b * args.steps / (ms_e2e / 1000.0), 3), "unit": UNIT,
+           "h2d_bytes_per_step": h_tok.numel() * 8 + h_codes.numel() * 8, "d2h_bytes_per_step": h_out.numel() * 8}
+
+    roof = roofline(eng, L, lens, dev, args)
+    line = None
+    if rank == 0:
+        nbytes, flops, _ = cfg1_bytes_flops(lens)
+        line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": cfg_dict(world), "roofline": roof, "e2e": e2e, "gpu_launches": int(launches) * args.steps,
+                "clocks": clk.summary(),
+                "step_roofline": {"bound": "hbm", "algorithmic_bytes": nbytes, "flops": flops,
+                                  "achieved_gbs": round(nbytes / (ms / args.steps / 1000.0) / 1e9, 1)}}
+        if world == 1 and not args.no_cpu:
+            v, cores, dt = cpu_sample(args.cpu_steps)
+            line["cpu_baseline"] = {"value": round(v, 3), "unit": UNIT, "cores": cores, "kind": "port",
+                                    "sample": f"{args.cpu_steps} cfg1 steps on the CPU oracle ({dt:.1f} s)"}
+    if world > 1:
+        dist.barrier()
+    del graph
+    return line
+
+
+def roofline(eng, L, lens, dev, args):
+    """Per-launch timing of the step's dominant kernels, each recorded for its 24 layers into a graph and timed with
+    CUDA events on the stream it runs on: split-K decode attention (HBM: the KV it reads) and the w13 GEMM
+    (HBM: its weights). Returns the one with the larger total time, with its achieved fraction of the peak."""
+    import ctypes as C
+
+    import torch
+    hbm, _, kind = _peaks()
+    b = B_CFG1
+    st = eng.slow
+    lens_d = lens.to(torch.int32).to(dev)
+    sc = eng.scratch
+    out = {}
+
+    def timed(fn, n_launch):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            fn()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(3, args.steps // 2)
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        z.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(z) / (reps * n_launch) / 1000.0     # seconds per launch
+
+    def attn_all():
+        for l in range(st.layers):
+            L.call("a8_attention", L.ptr(sc.q), 896, L.ptr(st.kc), L.ptr(st.vc), st.layers, st.cache_rows, 14, 2, 64,
+                   st.cache_len, l, L.ptr(lens_d), None, b, st.cache_len, 0.0, L.ptr(sc.o), 896, L.ptr(sc.attn_ws),
+                   sc.attn_ws.numel(), L.ptr(sc.attn_counters), sc.attn_counters.numel(), L.stream_handle())
+
+    def w13_all():
+        e = L.A8Epilogue(kind=L.EPI_SILU)
+        for l in range(st.layers):
+            L.call("a8_gemm", L.ptr(sc.h), 896, C.c_void_p(st.w13[l].data_ptr()), 2 * st.inter, 896, b, L.ptr(sc.mlp),
+                   st.inter, C.byref(e), 0, L.stream_handle())
+
+    t_attn = timed(attn_all, st.layers)
+    kv_bytes = 2 * 2 * 64 * 2 * int(lens.sum()) + b * 14 * 64 * 2 * 2
+    t_w13 = timed(w13_all, st.layers)
+    w13_bytes = 2 * st.inter * 896 * 2 + b * (896 + st.inter) * 2
+    cand = {"attention": (t_attn, kv_bytes), "w13_gemm": (t_w13, w13_bytes)}
+    name = max(cand, key=lambda k: cand[k][0])
+    t, nbytes = cand[name]
+    achieved = nbytes / t / 1e9
+    traffic = None
+    tp = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        tr = json.load(open(tp)).get(name)
+        if tr:
+            traffic = int(tr["bytes_per_unit"] * (int(lens.sum()) if name == "attention" else 1))
+    return {"kernel": name, "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(achieved / hbm, 4), "peak_kind": kind, "traffic": traffic,
+            "algorithmic_bytes_per_launch": nbytes, "us_per_launch": round(t * 1e6, 2),
+            "others": {k: {"us_per_launch": round(v[0] * 1e6, 2), "gbs": round(v[1] / v[0] / 1e9, 1)}
+                       for k, v in cand.items() if k != name}}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="cfg1", choices=["cfg1"])
+    ap.add_argument("--cpu-steps", type=int, default=3)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    args.gpus = world if world > 1 else args.gpus
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    line = run_ours(args, rank, world, local)
+    if rank == 0 and line is not None:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -37,6 +37,9 @@ int a8_device_ok(void);
  * Synchronises the device. */
 int a8_get_error(int out[4]);
 int a8_clear_error(void);
+/* Kernels this library has launched (or recorded into a graph) in this process; a host-side count, no device sync.
+ * No counterpart in the reference (a benchmark aid). */
+long long a8_launch_count(void);
 
 /* ---------------------------------------------------------------------------------------------- GEMM */
 /* Epilogue kinds of a8_gemm. Y = X[M,K] . W[N,K]^T accumulated in fp32 on the tensor cores (tcgen05, TMEM). */
@@ -68,14 +71,12 @@ typedef struct A8Epilogue {
   int ldres;
 } A8Epilogue;
 
-/* Workspace of a8_gemm for a shape (splits 0 = automatic). ws_floats / n_counters may be 0 (no split-K). */
-int a8_gemm_workspace(int N, int K, int M, int splits, long long* ws_floats, int* n_counters);
-
 /* y = epilogue(x[M, K] . w[N, K]^T). x row stride ldx, w dense; bf16. Replaces GemmDispatch / linear_triton
  * (serve/fast_kernels.py:364-520) and, through the epilogues, bias_rope_store (:139-187) and silu_mul (:526-545).
- * ws / counters: split-K scratch from a8_gemm_workspace (counters zeroed once before first use). */
+ * splits: K splits of a 128-row weight tile (0 = automatic, at most 16); the splits of a tile run as one thread-block
+ * cluster and add their partial sums through distributed shared memory, in split order (no global scratch). */
 int a8_gemm(const void* x, int ldx, const void* w, int N, int K, int M, void* y, int ldy, const A8Epilogue* epi,
-            float* ws, long long ws_floats, int* counters, int n_counters, int splits, a8_stream_t stream);
+            int splits, a8_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------------- attention */
 /* Workspace of a8_attention / a8_stack_forward's attention for `rows` query rows whose key count is at most max_len. */
@@ -121,10 +122,6 @@ typedef struct A8Scratch {
   void* o;              /* bf16 [rows, nq * hd] */
   void* a;              /* bf16 [rows, dim] */
   void* mlp;            /* bf16 [rows, inter] */
-  float* ws;            /* GEMM split-K partials (a8_gemm_workspace) */
-  long long ws_floats;
-  int* counters;        /* zeroed once */
-  int n_counters;
   float* attn_ws;       /* attention split partials (a8_attention_workspace) */
   long long attn_ws_floats;
   int* attn_counters;   /* zeroed once */

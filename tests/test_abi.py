@@ -13,7 +13,7 @@ HEADER = os.path.join(REPO, "include", "audio8_b200.h")
 def declared():
     src = open(HEADER).read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"\bint\s+(a8_\w+)\s*\(", src)))
+    return sorted(set(re.findall(r"\b(?:int|long long)\s+(a8_\w+)\s*\(", src)))
 
 
 def test_header_declares_entry_points():

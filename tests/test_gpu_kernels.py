@@ -42,8 +42,8 @@ def frac_equal(a, b):
 def gemm(L, ws, x, w, y, epi, splits=0, ldy=None):
     M, K = x.shape
     N = w.shape[0]
-    L.call("a8_gemm", L.ptr(x), x.stride(0), L.ptr(w), N, K, M, L.ptr(y), ldy or y.stride(0), C.byref(epi),
-           L.ptr(ws[0]), ws[0].numel(), L.ptr(ws[1]), ws[1].numel(), splits, L.stream_handle())
+    L.call("a8_gemm", L.ptr(x), x.stride(0), L.ptr(w), N, K, M, L.ptr(y), ldy or y.stride(0), C.byref(epi), splits,
+           L.stream_handle())
     torch.cuda.synchronize()
     assert L.device_error()[0] == 0, L.device_error()
 
