@@ -71,6 +71,8 @@ SIGNATURES = {
     "a8_attention": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                              c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_int, c_void_p, c_ll, c_void_p,
                              c_int, c_void_p]),
+    "a8_attention_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
+                                     c_int, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_int, c_void_p]),
     "a8_rmsnorm": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_float,
                            c_void_p]),
     "a8_embed_frame": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,

@@ -386,3 +386,39 @@ extern "C" int a8_attention(const void* q, int q_stride, const void* kc, const v
   a.rows = rows;
   return attn_launch(mk, mv, a, hd, group, reinterpret_cast<cudaStream_t>(stream));
 }
+
+// ------------------------------------------------------------------------------------------------ allocation-free
+// a8_attention for callers that cannot allocate device memory: the split workspace (partials and tickets) lives in
+// a fixed array of this library instead of caller memory. The array is a host-side stand-in in host code; its device
+// address comes from cudaGetSymbolAddress, taken once per device with that device current, on the first call.
+namespace a8 {
+static __device__ __align__(256) float g_attn_noalloc[A8_ATTENTION_NOALLOC_FLOATS];
+static float* g_attn_noalloc_dev[64];   // device address of g_attn_noalloc, per device ordinal
+}  // namespace a8
+
+extern "C" int a8_attention_noalloc(const void* q, int q_stride, const void* kc, const void* vc, int layers,
+                                    int cache_rows, int nq, int nkv, int hd, int cache_len, int layer, const int* lens,
+                                    const int* rowmap, int rows, int max_len, float scale, void* out, int out_stride,
+                                    a8_stream_t stream) {
+  if (rows <= 0 || nkv <= 0 || (hd != 64 && hd != 128) || max_len <= 0) return A8_ERR_ARG;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return A8_ERR_DEVICE;
+  if (g_attn_noalloc_dev[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_attn_noalloc) != cudaSuccess || p == nullptr) return A8_ERR_CUDA;
+    g_attn_noalloc_dev[dev] = reinterpret_cast<float*>(p);
+  }
+  const int chunk = attn_chunk(hd);
+  const int ms = (max_len + chunk - 1) / chunk;
+  const long long partials = ms > 1 ? attn_ws_floats(rows, nkv, ms, hd) : 0;
+  const long long tickets = ms > 1 ? (long long)rows * nkv : 0;
+  if (partials + tickets > A8_ATTENTION_NOALLOC_FLOATS) return A8_ERR_SIZE;
+  float* ws = g_attn_noalloc_dev[dev];
+  int* counters = reinterpret_cast<int*>(ws + partials);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // the tickets must start at zero: the array keeps whatever the previous call left
+  if (tickets > 0 && cudaMemsetAsync(counters, 0, tickets * sizeof(int), s) != cudaSuccess) return A8_ERR_CUDA;
+  return a8_attention(q, q_stride, kc, vc, layers, cache_rows, nq, nkv, hd, cache_len, layer, lens, rowmap, rows,
+                      max_len, scale, out, out_stride, ms > 1 ? ws : nullptr, partials, ms > 1 ? counters : nullptr,
+                      (int)tickets, stream);
+}

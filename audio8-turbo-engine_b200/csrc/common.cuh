@@ -10,6 +10,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/audio8_b200.h"
+
 #ifndef A8_WAIT_LIMIT_NS
 #define A8_WAIT_LIMIT_NS 2000000000ull  // 2 s: far above any legitimate wait in these kernels
 #endif

@@ -91,6 +91,24 @@ int a8_attention(const void* q, int q_stride, const void* kc, const void* vc, in
                  float scale, void* out, int out_stride, float* ws, long long ws_floats, int* counters, int n_counters,
                  a8_stream_t stream);
 
+/* Size of the library-owned workspace of a8_attention_noalloc, in 4-byte words (8 MiB). */
+#define A8_ATTENTION_NOALLOC_FLOATS (1 << 21)
+
+/* a8_attention without caller-provided scratch. No counterpart in the reference: it exists for callers that cannot
+ * allocate device memory -- a host-language binding that is handed only the device pointers of its inputs and outputs
+ * and has no CUDA allocator of its own, or a serving process whose memory pool already owns the whole device -- and
+ * so cannot supply the workspace a8_attention needs when a row's keys span several splits.
+ * The split partials and tickets live in one array inside this library (8 MiB, held on every device that loads the
+ * library until the process exits). A call needs rows * nkv * S * (16 hd + 32) + rows * nkv words of it when S > 1
+ * splits (S = ceil(max_len / 256) for hd 64, ceil(max_len / 128) for hd 128); larger requests return A8_ERR_SIZE.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress, with that device current):
+ * make that first call before any stream capture. Every call shares the array and it keeps the last call's contents;
+ * the tickets are cleared (cudaMemsetAsync on the given stream) at each call. Calls that overlap on the GPU (other
+ * streams, other threads, the same device) race on the array. Allocates nothing. */
+int a8_attention_noalloc(const void* q, int q_stride, const void* kc, const void* vc, int layers, int cache_rows,
+                         int nq, int nkv, int hd, int cache_len, int layer, const int* lens, const int* rowmap,
+                         int rows, int max_len, float scale, void* out, int out_stride, a8_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------------- row kernels */
 /* y = bf16(w * bf16(h * rsqrt(mean(h^2) + eps))), h = bf16(x + res) stored back into res (res may be NULL: h = x).
  * N <= 1024, a multiple of 8. Replaces rmsnorm (serve/fast_kernels.py:30-69). */
