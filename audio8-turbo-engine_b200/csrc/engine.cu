@@ -7,8 +7,8 @@ namespace a8 {
 
 int attn_maps(CUtensorMap* mk, CUtensorMap* mv, const void* kc, const void* vc, long long total_rows, int hd);
 int attn_launch(const CUtensorMap& mk, const CUtensorMap& mv, AttnArgs a, int hd, int group, cudaStream_t s);
-int attn_chunk(int hd);
-long long attn_ws_floats(int rows, int nkv, int max_splits, int hd);
+int attn_splits(int rows, int nkv, int max_len);
+long long attn_ws_floats(int rows, int nkv, int nsplit, int hd);
 int sample_launch(const SampleArgs& a, int rows, cudaStream_t s);
 
 #define A8_TRY(x)              \
@@ -54,9 +54,8 @@ int stack_forward(const A8StackDesc& d, const A8StackRun& r, cudaStream_t s) {
   CUtensorMap mk, mv;
   const long long total = (long long)d.layers * d.cache_rows * d.nkv * d.cache_len;
   A8_TRY(attn_maps(&mk, &mv, d.kc, d.vc, total, d.hd));
-  const int chunk = attn_chunk(d.hd);
   const int max_len = r.max_len > 0 ? r.max_len : d.cache_len;
-  const int ms = (max_len + chunk - 1) / chunk;
+  const int ms = attn_splits(R, d.nkv, max_len);
   if (ms > 1 && (sc.attn_ws == nullptr || sc.attn_ws_floats < attn_ws_floats(R, d.nkv, ms, d.hd) ||
                  sc.attn_counters == nullptr || sc.n_attn_counters < R * d.nkv))
     return A8_ERR_SIZE;
@@ -87,7 +86,7 @@ int stack_forward(const A8StackDesc& d, const A8StackRun& r, cudaStream_t s) {
     aa.rowmap = r.rowmap;
     aa.cache_rows_per_layer_head = d.cache_len;
     aa.layer_base = (long long)l * d.cache_rows * d.nkv * d.cache_len;
-    aa.max_splits = ms;
+    aa.nsplit = ms;
     aa.scale_log2 = (1.0f / sqrtf((float)d.hd)) * 1.4426950408889634f;
     aa.out = o;
     aa.out_stride = QW;

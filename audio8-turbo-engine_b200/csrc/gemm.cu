@@ -209,8 +209,16 @@ __global__ void __launch_bounds__(128, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int stages = a.stages;
   const uint32_t stage_bytes = TILE_A_BYTES + a.ntok * BK * 2;
-  const uint32_t reduce_bytes = a.splits > 1 ? ((a.ntok + 31) / 32 * 32) * 128 * 4 + 32 * STAGE_PITCH * 4 : 0;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + max(stages * stage_bytes, reduce_bytes));
+  // [pipeline slots][cluster split-K: receive buffer S x w x 128 fp32][reduced slice 32 x STAGE_PITCH][barriers]
+  const int ntok32 = (a.ntok + 31) / 32 * 32;
+  const int S = a.splits;
+  const int w = (ntok32 + S - 1) / S;                       // token columns each cluster rank reduces
+  const uint32_t pipe_bytes = stages * stage_bytes;
+  const uint32_t recv_bytes = S > 1 ? uint32_t(S * w * 128 * 4) : 0u;
+  const uint32_t slice_bytes = S > 1 ? uint32_t(32 * STAGE_PITCH * 4) : 0u;
+  float* recv = reinterpret_cast<float*>(smem + pipe_bytes);
+  float* slice = reinterpret_cast<float*>(smem + pipe_bytes + recv_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + pipe_bytes + recv_bytes + slice_bytes);
   uint64_t* empty = full + stages;
   uint64_t* accum = empty + stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
@@ -307,43 +315,37 @@ __global__ void __launch_bounds__(128, 1)
       __syncthreads();
     }
   } else {
-    // The K splits of this tile form one cluster (blockIdx.z = rank). Each CTA leaves its fp32 partial [ntok32][128]
-    // in its own shared memory; after a cluster barrier CTA `rank` reduces token columns [c0, c1) over all peers
-    // through distributed shared memory, in split order (deterministic), and runs the epilogue on them.
-    const int ntok32 = nchunk * 32;
-    float* part = reinterpret_cast<float*>(smem);
-    float* slice = part + ntok32 * 128;                     // [32][STAGE_PITCH] reduced columns of this CTA
+    // The K splits of this tile form one cluster (blockIdx.z = rank). Token column col belongs to rank col / w:
+    // every CTA pushes its fp32 partial of each column into the owner's receive buffer recv[rank][col - owner w][row]
+    // with remote stores, then one cluster barrier, then each owner adds its columns over the ranks in split order
+    // (deterministic) from its own shared memory and runs the epilogue on them. The receive buffer is not part of the
+    // pipeline slots: a peer may push while this CTA is still in its mainloop.
+    const uint32_t recv_local = smem_u32(recv);
     for (int c = 0; c < nchunk; ++c) {
       float v[32];
       tmem_ld32(trow + c * 32, v);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) part[(c * 32 + i) * 128 + row] = ok ? v[i] : 0.f;
+      for (int i = 0; i < 32; ++i) {
+        const int col = c * 32 + i;
+        const int owner = col / w;
+        const uint32_t off = uint32_t(((split * w + (col - owner * w)) * 128 + row) * 4);
+        dsmem_st(dsmem_addr(recv_local + off, owner), ok ? v[i] : 0.f);
+      }
     }
     cluster_sync();
-    const int S = a.splits;
-    const int w = (ntok32 + S - 1) / S;
     const int c0 = min(ntok32, split * w), c1 = min(ntok32, c0 + w);
-    uint32_t peer[16];
-#pragma unroll
-    for (int p = 0; p < 16; ++p) peer[p] = p < S ? dsmem_addr(smem_u32(part), p) : 0u;
     for (int cc = c0; cc < c1; cc += 32) {                   // the slice buffer and the epilogue take 32 columns
       const int ce = min(c1, cc + 32);
       for (int col = cc; col < ce; ++col) {
-        const uint32_t off = uint32_t(col * 128 + row) * 4u;
-        float v[16];
-#pragma unroll
-        for (int p = 0; p < 16; ++p) v[p] = p < S ? dsmem_ld(peer[p] + off) : 0.f;
+        const int j = col - c0;
         float s = 0.f;
-#pragma unroll
-        for (int p = 0; p < 16; ++p)
-          if (p < S) s += v[p];
+        for (int p = 0; p < S; ++p) s += recv[(p * w + j) * 128 + row];
         slice[(col - cc) * STAGE_PITCH + row] = s;
       }
       __syncthreads();
       run_epilogue<KIND>(a, slice, n0, m0 + cc, m0 + ce, tid);
       __syncthreads();
     }
-    cluster_sync();                                          // peers have read this CTA's partial
   }
   tc_fence_before();
   __syncthreads();
@@ -495,13 +497,16 @@ int gemm_plan(GemmPlan* p, const void* x, int ldx, const void* w, int N, int K, 
   const int stage_bytes = TILE_A_BYTES + a.ntok * BK * 2;
   const int budget = 200 * 1024;
   const int ntok32 = (a.ntok + 31) / 32 * 32;
-  const int reduce_bytes = ntok32 * 128 * 4 + 32 * STAGE_PITCH * 4;   // cluster split-K: partial + reduced slice
   int smem = 0;
   for (;;) {
-    a.stages = std::max(2, std::min(8, budget / stage_bytes));
+    // cluster split-K: receive buffer (S x w x 128 fp32) + reduced slice beside the pipeline slots
+    const int w = (ntok32 + a.splits - 1) / a.splits;
+    const int reduce_bytes = a.splits > 1 ? a.splits * w * 128 * 4 + 32 * STAGE_PITCH * 4 : 0;
+    a.stages = std::max(2, std::min(8, (budget - reduce_bytes) / stage_bytes));
     a.stages = std::min(a.stages, std::max(2, a.kb_per_split));
-    smem = std::max(a.stages * stage_bytes, a.splits > 1 ? reduce_bytes : 0) + 1024 + 256;
-    if (a.splits == 1 || cluster_fits(epi->kind, smem, a.splits)) break;
+    smem = a.stages * stage_bytes + reduce_bytes + 1024 + 256;
+    const bool fits = smem <= 227 * 1024 && (a.splits == 1 || cluster_fits(epi->kind, smem, a.splits));
+    if (fits || a.splits == 1) break;
     const int s = std::max(1, a.splits / 2);         // a cluster that cannot be resident: halve it
     a.kb_per_split = (a.kb_total + s - 1) / s;
     a.splits = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;

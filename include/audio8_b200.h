@@ -79,7 +79,8 @@ int a8_gemm(const void* x, int ldx, const void* w, int N, int K, int M, void* y,
             int splits, a8_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------------- attention */
-/* Workspace of a8_attention / a8_stack_forward's attention for `rows` query rows whose key count is at most max_len. */
+/* Workspace of a8_attention / a8_stack_forward's attention for calls of up to `rows` query rows whose key count is at
+ * most max_len (fewer rows are split into more parts, so this is the largest need over 1..rows rows). */
 int a8_attention_workspace(int rows, int nkv, int hd, int max_len, long long* ws_floats, int* n_counters);
 
 /* out[r, h, :] = softmax(q[r, h] . K[c, h / group, :L_r] * scale) V[c, h / group, :L_r], c = rowmap[r] (or r),
@@ -91,16 +92,17 @@ int a8_attention(const void* q, int q_stride, const void* kc, const void* vc, in
                  float scale, void* out, int out_stride, float* ws, long long ws_floats, int* counters, int n_counters,
                  a8_stream_t stream);
 
-/* Size of the library-owned workspace of a8_attention_noalloc, in 4-byte words (8 MiB). */
-#define A8_ATTENTION_NOALLOC_FLOATS (1 << 21)
+/* Size of the library-owned workspace of a8_attention_noalloc, in 4-byte words (4 MiB). */
+#define A8_ATTENTION_NOALLOC_FLOATS (1 << 20)
 
 /* a8_attention without caller-provided scratch. No counterpart in the reference: it exists for callers that cannot
  * allocate device memory -- a host-language binding that is handed only the device pointers of its inputs and outputs
  * and has no CUDA allocator of its own, or a serving process whose memory pool already owns the whole device -- and
  * so cannot supply the workspace a8_attention needs when a row's keys span several splits.
- * The split partials and tickets live in one array inside this library (8 MiB, held on every device that loads the
- * library until the process exits). A call needs rows * nkv * S * (16 hd + 32) + rows * nkv words of it when S > 1
- * splits (S = ceil(max_len / 256) for hd 64, ceil(max_len / 128) for hd 128); larger requests return A8_ERR_SIZE.
+ * The split partials and tickets live in one array inside this library (4 MiB, held on every device that loads the
+ * library until the process exits). A call needs rows * nkv * S * (16 hd + 32) + rows * nkv words of it when its rows
+ * are split in S > 1 parts (S = min(16, ceil(max_len / 64), ceil(296 / (rows * nkv))), so at most about 0.65 M words);
+ * a request beyond the array returns A8_ERR_SIZE.
  * The first call on a device looks up the array's device address (cudaGetSymbolAddress, with that device current):
  * make that first call before any stream capture. Every call shares the array and it keeps the last call's contents;
  * the tickets are cleared (cudaMemsetAsync on the given stream) at each call. Calls that overlap on the GPU (other

@@ -60,12 +60,3 @@ def test_noalloc_attention_matches_workspace_version_twice(L, a8):
         assert not torch.isnan(got.float()).any()
         rel = float((got.float() - ref.float()).abs().max() / ref.float().abs().max())
         assert rel < 1e-2, rel
-
-
-def test_noalloc_attention_rejects_requests_beyond_its_array(L):
-    q, kc, vc, lens, dims = _case(13, 4, 64)
-    nq, nkv, hd, S, layers = dims
-    rows = 2000                                   # 2000 rows x 2 heads x 8 splits x 1056 words > 2^21 words
-    rc = L.load().a8_attention_noalloc(L.ptr(q), nq * hd, L.ptr(kc), L.ptr(vc), layers, 5, nq, nkv, hd, S, 0,
-                                       L.ptr(lens), None, rows, S, 0.0, L.ptr(q), nq * hd, L.stream_handle())
-    assert rc == 4                                # A8_ERR_SIZE, before anything is launched
