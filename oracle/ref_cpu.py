@@ -111,9 +111,18 @@ def bias_rope_store(qkv, bias, cos, sin, pos, slot, kc, vc, nq, nkv, hd, ring=1 
     return q
 
 
+def _softmax_pv(s, v, eq):
+    """softmax(s) V with the reference's rounding point: the unnormalised weights exp(s - max) are rounded to bf16 for
+    the P.V product, the normaliser sums them unrounded (serve/fast_kernels.py:225-230, :253). The reference takes the
+    max per 64-key block and rescales; the oracle takes the row max (identical for rows of up to 64 keys)."""
+    e = torch.exp(s - s.max(-1, keepdim=True).values)
+    return torch.einsum(eq, bf(e), v) / e.sum(-1, keepdim=True)
+
+
 def decode_attention(q, kc, vc, lens, rowmap=None, scale=None):
-    """One query per row, GQA: out[r, h] = softmax(q . K[crow, h//group, :L] * scale) V, exact in fp32, rounded to
-    bf16. serve/fast_kernels.py:193-253 (split-K flash decoding; the split merge is exact up to rounding)."""
+    """One query per row, GQA: out[r, h] = softmax(q . K[crow, h//group, :L] * scale) V in fp32 (weights rounded to
+    bf16 for P.V), rounded to bf16. serve/fast_kernels.py:193-253 (split-K flash decoding; the split merge is exact up
+    to rounding)."""
     b, nq, hd = q.shape
     nkv = kc.shape[1]
     g = nq // nkv
@@ -126,8 +135,7 @@ def decode_attention(q, kc, vc, lens, rowmap=None, scale=None):
         v = vc[cr, :, :L].float()
         qq = q[r].float().view(nkv, g, hd)
         s = torch.einsum("hgd,hnd->hgn", qq, k) * scale
-        p = torch.softmax(s, -1)
-        out[r] = torch.einsum("hgn,hnd->hgd", p, v).reshape(nq, hd)
+        out[r] = _softmax_pv(s, v, "hgn,hnd->hgd").reshape(nq, hd)
     return bf(out)
 
 
@@ -150,8 +158,7 @@ def prefill_attention(q, kc, vc, blocks, scale=None):
         s = torch.einsum("nhgd,hkd->nhgk", qq, k) * scale
         qpos = torch.arange(p0, p0 + n).view(n, 1, 1, 1)
         s = s.masked_fill(torch.arange(hi).view(1, 1, 1, hi) > qpos, float("-inf"))
-        p = torch.softmax(s, -1)
-        out[q0:q0 + n] = torch.einsum("nhgk,hkd->nhgd", p, v).reshape(n, nq, hd)
+        out[q0:q0 + n] = _softmax_pv(s, v, "nhgk,hkd->nhgd").reshape(n, nq, hd)
     return bf(out)
 
 
@@ -309,7 +316,10 @@ def snake(x, alpha, ib):
 
 class Conv:
     """_CLConv (serve/fast_engine.py:178-232): channels-last causal conv or polyphase transposed conv on fp16
-    values, with its activated left context carried per row."""
+    values, with its activated left context carried per row. `Conv.f16acc_bk` (class switch, default 0): emulate the
+    reference kernel's fp16 accumulation of each BK-channel slice instead of the exact fp32 sum."""
+
+    f16acc_bk = 0
 
     def __init__(self, m, Bmax, snake_mod=None, trans=False):
         c = m.conv
@@ -345,7 +355,14 @@ class Conv:
         for p in range(self.ph):
             acc = torch.zeros(b, T, self.Cout)
             for j in range(self.taps):
-                acc = acc + xin[:, j * self.dil:j * self.dil + T] @ self.W[p, j]
+                xs = xin[:, j * self.dil:j * self.dil + T]
+                if Conv.f16acc_bk:
+                    # the reference's F16ACC: each BK-channel slice's dot product rounded to fp16 before the fp32
+                    # accumulation (serve/fast_kernels.py:585-586); off by default (the exact decode)
+                    for c0 in range(0, self.Cin, Conv.f16acc_bk):
+                        acc = acc + hf(xs[..., c0:c0 + Conv.f16acc_bk] @ self.W[p, j, c0:c0 + Conv.f16acc_bk])
+                else:
+                    acc = acc + xs @ self.W[p, j]
             y[:, :, p] = acc
         y = y.reshape(b, T * self.ph, self.Cout)
         if self.bias is not None:

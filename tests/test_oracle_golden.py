@@ -168,3 +168,72 @@ def test_stack(tiny_model):
     hd = st.forward(d["xd"].float(), d["dpos"], d["dslot"], d["dpos"] + 1, rowmap=True)
     assert rel(hd, d["h_dec"]) < 2e-2
     assert rel(st.kc, d["kc"]) < 2e-2 and rel(st.vc, d["vc"]) < 2e-2
+
+
+def snr_db(a, ref):
+    a, ref = a.double().flatten(), ref.double().flatten()
+    return float(10 * torch.log10((ref ** 2).sum() / ((a - ref) ** 2).sum().clamp(min=1e-30)))
+
+
+@pytest.mark.slow
+def test_vocoder_step(tiny_model):
+    """StreamingVocoder.step: table sum, 2-layer window transformer, two upsample stages, full-size DAC decoder with
+    carried conv state, 2 frames for 2 rows (reference run: its fp16 convs accumulate each BK slice in fp16)."""
+    d = golden("vocoder")
+    codec = tiny_model.load_codec("cpu", torch.float32)
+    v = R.Vocoder(codec, 2)
+    for t in range(d["codes"].shape[0]):
+        w = v.step(d["codes"][t], 2)
+        assert snr_db(w, d["wav"][t]) > 40, (t, snr_db(w, d["wav"][t]))
+    assert torch.equal(v.pos[:2], d["pos"][:2])
+
+
+def _ulp(v):
+    e = max(-126, int(np.floor(np.log2(max(abs(float(v)), 1e-30)))))
+    return 2.0 ** (e - 7)
+
+
+@pytest.mark.slow
+def test_engine_admit_and_ticks(tiny_model):
+    """FastEngine (bf16 model, greedy): admission (prefix KV per voice, packed prefill, first token) and 3 ticks with
+    the codec one frame behind. Each row is compared until its first difference, which must be a near-tie (within 2
+    bf16 ulps) of the oracle's own logits for that draw -- random weights give nearly flat logits. Until then: codes,
+    tokens and bookkeeping equal, logits within 2e-2, audio SNR > 40 dB."""
+    from types import SimpleNamespace
+    from oracle.standin import StubTokenizer
+    d = golden("engine")
+    gp = dict(do_sample=False, temperature=0.8, top_k=50, top_p=0.95, max_new_tokens=64)
+    ora = R.OracleEngine(tiny_model, StubTokenizer(), gp, max_slots=3, max_seq=512)
+    item = SimpleNamespace(ref_code=d["ref_code"], ref_text=d["ref_text"])
+    reqs = [dict(text=d["text"], item=item, key="v0"), dict(text=d["text2"], item=item, key="v0")]
+    ora.record = {}
+    assert ora.admit([0, 2], reqs) == d["lens"]
+    assert rel(ora.record["prefill_logits"][0], d["prefill_logits"][0]) < 2e-2
+    assert torch.equal(ora.tok, d["state0"]["tok"]) and torch.equal(ora.cpos, d["state0"]["cpos"])
+    live, ties = [True, True, True], []
+    for t in range(d["tok_in"].shape[0]):
+        ora.record = {}
+        codes = ora.tick(3)
+        for r in range(3):
+            if not live[r]:
+                continue
+            assert snr_db(ora.audio[r], d["audio"][t][r]) > 40, (t, r)
+            ref_codes = d["frame_prev"][t][r]
+            if int(d["tok_in"][t][r]) != ora.eos and not torch.equal(codes[r], ref_codes):
+                k = int((codes[r] != ref_codes).nonzero()[0])
+                lg = ora.record["fast_logits"][k - 1][r]
+                gap = float(lg[int(codes[r, k])] - lg[int(ref_codes[k])])
+                assert gap <= 2 * _ulp(lg[int(codes[r, k])]), (t, r, k, gap)
+                ties.append((t, r, k))
+                live[r] = False
+                continue
+            assert rel(ora.record["logits"][-1][r], d["logits"][t][r]) < 2e-2, (t, r)
+            for key in ("tok_in", "frame_prev", "cpos", "nstep", "prev"):
+                assert torch.equal(getattr(ora, key)[r], d[key][t][r]), (t, r, key)
+            if int(ora.tok[r]) != int(d["tok"][t][r]):
+                j = lambda tok: ora.nsem if int(tok) == ora.eos else int(tok) - ora.sb
+                lg = ora.record["logits"][-1][r]
+                assert float(lg[j(ora.tok[r])] - lg[j(d["tok"][t][r])]) <= 2 * _ulp(lg[j(ora.tok[r])]), (t, r)
+                ties.append((t, r, 0))
+                live[r] = False
+    assert sum(live) >= 1, ties
