@@ -45,6 +45,37 @@ class A8StackRun(C.Structure):
                 ("scratch", A8Scratch)]
 
 
+MAX_UPS, MAX_CONV_OPS = 4, 40
+STATE_CLEAR, STATE_LOAD, STATE_SNAPSHOT = 0, 1, 2
+
+
+class A8ConvOp(C.Structure):
+    _fields_ = [("w", c_void_p), ("bias", c_void_p), ("alpha", c_void_p), ("inv", c_void_p), ("state", c_void_p),
+                ("state_bs", c_ll), ("Cin", c_int), ("N", c_int), ("taps", c_int), ("dil", c_int), ("ctx", c_int),
+                ("T", c_int), ("in_", c_int), ("out", c_int), ("res", c_int)]
+
+
+class A8Upsample(C.Structure):
+    _fields_ = [("tw", c_void_p), ("tb", c_void_p), ("dww", c_void_p), ("dwb", c_void_p), ("st", c_void_p),
+                ("st_bs", c_ll), ("K", c_int), ("eps", c_float), ("lnw", c_void_p), ("lnb", c_void_p),
+                ("w1", c_void_p), ("b1", c_void_p), ("w2", c_void_p), ("b2", c_void_p), ("gamma", c_void_p),
+                ("mlp", c_int)]
+
+
+class A8Vocoder(C.Structure):
+    _fields_ = [("B", c_int), ("ncb", c_int), ("C", c_int), ("v_sem", c_int), ("v_res", c_int), ("max_pos", c_int),
+                ("window", c_int), ("up", c_int), ("t_sem", c_void_p), ("t_res", c_void_p), ("pos", c_void_p),
+                ("pos_c", c_void_p), ("lens", c_void_p), ("x", c_void_p), ("post", A8StackDesc),
+                ("scratch", A8Scratch), ("n_ups", c_int), ("ups", A8Upsample * MAX_UPS), ("ubuf", c_void_p * 4),
+                ("n_ops", c_int), ("ops", A8ConvOp * MAX_CONV_OPS), ("act", c_void_p * 3), ("xin", c_void_p),
+                ("audio", c_void_p)]
+
+
+class A8StateSeg(C.Structure):
+    _fields_ = [("base", c_void_p), ("slot_stride", c_ll), ("chunk_bytes", c_ll), ("chunk_stride", c_ll),
+                ("nchunks", c_int), ("blob_off", c_ll)]
+
+
 class A8Engine(C.Structure):
     _fields_ = [("B", c_int), ("S", c_int), ("H", c_int), ("ncb", c_int), ("cbk", c_int), ("nsem", c_int),
                 ("vocab", c_int), ("ras_w", c_int), ("eos", c_ll), ("sb", c_ll), ("do_sample", c_int),
@@ -56,7 +87,7 @@ class A8Engine(C.Structure):
                 ("sil_frame", c_void_p), ("tick_ctr", c_void_p), ("tick_id", c_void_p), ("x_fast2", c_void_p),
                 ("x_fast", c_void_p), ("x_slow", c_void_p), ("codes", c_void_p), ("logits", c_void_p),
                 ("ld_logits", c_int), ("f_pos", c_void_p), ("f_pos0", c_void_p), ("f_slot0", c_void_p),
-                ("scratch", A8Scratch)]
+                ("scratch", A8Scratch), ("voc", C.POINTER(A8Vocoder)), ("side", c_void_p)]
 
 
 # name -> (restype, argtypes)
@@ -82,6 +113,16 @@ SIGNATURES = {
     "a8_gather_rows": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "a8_sample": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_float, c_float, c_ull, c_int, c_void_p,
                           c_void_p, c_void_p]),
+    "a8_conv": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
+                        c_ll, c_ll, c_void_p, c_ll, c_ll, c_int, c_void_p]),
+    "a8_snake_cat": (c_int, [c_void_p, c_int, c_ll, c_int, c_int, c_void_p, c_ll, c_int, c_void_p, c_void_p,
+                             c_void_p, c_int, c_void_p]),
+    "a8_ups_dwln": (c_int, [c_void_p, c_int, c_int, c_void_p, c_ll, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+                            c_float, c_void_p, c_int, c_void_p]),
+    "a8_codec_embed": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                               c_void_p, c_int, c_int, c_int, c_void_p]),
+    "a8_voc_step": (c_int, [C.POINTER(A8Vocoder), c_void_p, c_int, c_void_p]),
+    "a8_state_rows": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "a8_stack_forward": (c_int, [C.POINTER(A8StackDesc), C.POINTER(A8StackRun), c_void_p]),
     "a8_tick": (c_int, [C.POINTER(A8Engine), c_int, c_void_p]),
     "a8_slow_step": (c_int, [C.POINTER(A8Engine), c_int, c_void_p]),

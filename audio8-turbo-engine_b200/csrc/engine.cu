@@ -220,11 +220,48 @@ int slow_step(const A8Engine& e, int b, cudaStream_t s) {
   return sample_launch(sa, b, s);
 }
 
+// Events of the tick's fork / join with the codec's stream, one set per device (created at the first tick with a
+// codec, which must run outside stream capture; a captured graph keeps only the dependencies they express).
+struct TickEvents {
+  cudaEvent_t fork = nullptr, read = nullptr, join = nullptr;
+};
+static int tick_events(TickEvents** out) {
+  static TickEvents ev[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return A8_ERR_CUDA;
+  TickEvents& t = ev[dev];
+  if (t.fork == nullptr) {
+    if (cudaEventCreateWithFlags(&t.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&t.read, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&t.join, cudaEventDisableTiming) != cudaSuccess)
+      return A8_ERR_CUDA;
+  }
+  *out = &t;
+  return A8_OK;
+}
+
+// FastEngine._tick (serve/fast_engine.py:737-769): the codec decodes the PREVIOUS tick's frame (frame_prev) on the
+// side stream while this stream runs the fast AR and the slow step; the semantic draw, which rewrites frame_prev,
+// waits until the codec has read it, and the tick ends when both streams have.
 int tick(const A8Engine& e, int b, cudaStream_t s) {
   A8_TRY(a8_tick_start(e.tok, e.tok_in, e.codes, e.ncb, e.sb, e.cbk, e.hid, e.fast_emb, e.x_fast2, b, e.H,
                        e.tick_ctr, e.tick_id, reinterpret_cast<a8_stream_t>(s)));
+  TickEvents* ev = nullptr;
+  const bool codec = e.voc != nullptr;
+  cudaStream_t side = reinterpret_cast<cudaStream_t>(e.side);
+  if (codec) {
+    if (side == nullptr || side == s) return A8_ERR_ARG;
+    A8_TRY(tick_events(&ev));
+    if (cudaEventRecord(ev->fork, s) != cudaSuccess || cudaStreamWaitEvent(side, ev->fork, 0) != cudaSuccess)
+      return A8_ERR_CUDA;
+    A8_TRY(voc_step(*e.voc, e.frame_prev, b, side, ev->read));
+    if (cudaEventRecord(ev->join, side) != cudaSuccess) return A8_ERR_CUDA;
+  }
   A8_TRY(fast_ar(e, b, s));
-  return slow_step(e, b, s);
+  if (codec && cudaStreamWaitEvent(s, ev->read, 0) != cudaSuccess) return A8_ERR_CUDA;
+  A8_TRY(slow_step(e, b, s));
+  if (codec && cudaStreamWaitEvent(s, ev->join, 0) != cudaSuccess) return A8_ERR_CUDA;
+  return A8_OK;
 }
 
 // Admission tail (serve/fast_engine.py:1124-1133, :828-835): logits of each request's last prompt row -> its first

@@ -3,4 +3,7 @@
 #include "attention.cu"
 #include "rowops.cu"
 #include "sample.cu"
+#include "conv.cu"
+#include "codec.cu"
+#include "vocoder.cu"
 #include "engine.cu"

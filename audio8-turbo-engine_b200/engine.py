@@ -172,14 +172,23 @@ class FastEngine:
         self.head = head.to(dev)
         self.fast_emb = f32(model.fast_embeddings.weight).to(BF16).to(dev)
         self.fast_out = f32(model.fast_output.weight).to(BF16).to(dev)
-        self.sr = int(getattr(c, "codec_sample_rate", 44100))
-        self.up = 2048
+        # codec: built from an fp32 copy of the model's codec (serve/fast_engine.py:625-633)
+        from .codec import StreamingVocoder
+        with torch.no_grad():                             # (not inference tensors: callers may write the state)
+            codec = model.load_codec(device=dev, dtype=torch.float32)
+            self.sr = int(getattr(codec, "sample_rate", getattr(c, "codec_sample_rate", 44100)))
+            self.voc = StreamingVocoder(codec, B, dev, max_pos=int(os.environ.get("TTS_VOC_MAX_POS", "8192")))
+            del codec
+        self.up = self.voc.up
         self.fps = self.sr / self.up
         codes, _ = model.encode_audio(torch.zeros(1, 1, self.sr, device=model.device))
         self.sil_frame = codes[0, :, codes.shape[-1] // 2].long().clamp(min=0).to(dev)
-        self.voc = None
-        self.voc_snaps = {}
-        self.voc_prime = False
+        # TTS_VOC_PRIME=0 (default): a row's codec starts clean and decodes a silence frame first; 1: from a snapshot
+        # of its voice's reference decoded (prime_speakers)
+        self.voc_prime = os.environ.get("TTS_VOC_PRIME", "0").strip().lower() not in ("0", "false", "no", "off")
+        self.prime_frames = max(2, int(os.environ.get("TTS_VOC_PRIME_FRAMES", "160")))
+        self.voc_snaps: Dict[str, tuple] = {}
+        self.side = torch.cuda.Stream(device=dev)
 
         # persistent per-slot state (fixed addresses; row B = SCR, prefill padding)
         i64, i32 = torch.int64, torch.int32
@@ -189,7 +198,7 @@ class FastEngine:
         self.prev = torch.zeros(B + 1, self.ras_w, dtype=i64, device=dev)
         self.nstep = torch.zeros(B + 1, dtype=i32, device=dev)
         self.tok_in = torch.zeros(B, dtype=i64, device=dev)
-        self.audio = torch.zeros(B, self.up, dtype=torch.float32, device=dev)
+        self.audio = self.voc.audio                       # [B, up] fp32: the codec writes it in the tick
         self.frame_prev = torch.zeros(B, self.ncg, dtype=i64, device=dev)
         self.tick_ctr = torch.zeros(1, dtype=i64, device=dev)
         self.tick_id = torch.zeros(1, dtype=i64, device=dev)
@@ -224,7 +233,8 @@ class FastEngine:
             tick_ctr=L.ptr(self.tick_ctr), tick_id=L.ptr(self.tick_id), x_fast2=L.ptr(self.x_fast2),
             x_fast=L.ptr(self.x_fast), x_slow=L.ptr(self.x_slow), codes=L.ptr(self.codes), logits=L.ptr(self.logits),
             ld_logits=self.ld_logits, f_pos=L.ptr(self.f_pos), f_pos0=L.ptr(self.f_pos0),
-            f_slot0=L.ptr(self.f_slot0), scratch=self.scratch.desc)
+            f_slot0=L.ptr(self.f_slot0), scratch=self.scratch.desc, voc=C.pointer(self.voc.desc),
+            side=C.c_void_p(self.side.cuda_stream))
 
         env_b = os.environ.get("TTS_BATCH_BUCKETS", "").strip()
         if env_b:
@@ -271,8 +281,9 @@ class FastEngine:
         log(f"[a8] captured {len(self.graphs)} tick graphs {self.buckets} in {time.perf_counter() - t0:.1f}s")
 
     def reset_state(self):
-        for t in (self.tok, self.cpos, self.hid, self.prev, self.nstep, self.tick_ctr, self.frame_prev):
+        for t in (self.tok, self.cpos, self.hid, self.prev, self.nstep, self.tick_ctr, self.frame_prev, self.audio):
             t.zero_()
+        self.voc.clear_many(list(range(self.B)))
 
     def bucket_for(self, n_rows):
         for b in self.buckets:
@@ -393,9 +404,44 @@ class FastEngine:
     def prime_speaker(self, key, item):
         self.prime_speakers([(key, item)])
 
+    @torch.inference_mode()
     def prime_speakers(self, pairs):
-        """TTS_VOC_PRIME=0 (the reference's default): rows start with a clean codec state, nothing to prime."""
-        return None
+        """serve/fast_engine.py:994-1033: up to B voice references decode side by side through the codec (rows
+        [0, B), only while nothing runs), each row snapshotted after its own second-to-last frame; the snapshot (host,
+        pinned) and the last frame are kept per key. TTS_VOC_PRIME=0 (default): nothing to do."""
+        if not self.voc_prime:
+            return
+        todo, seen = [], set()
+        for key, item in pairs:
+            if key not in self.voc_snaps and key not in seen:
+                seen.add(key)
+                todo.append((key, item))
+        for g in range(0, len(todo), self.B):
+            grp = todo[g:g + self.B]
+            n = len(grp)
+            codes = []
+            for _, item in grp:
+                rc = getattr(item, "ref_code", None)
+                if rc is not None:
+                    rc = rc[-self.prime_frames:]
+                codes.append(rc.to(self.dev).long() if rc is not None and rc.shape[0] > 0
+                             else torch.zeros(0, self.ncg, dtype=torch.long, device=self.dev))
+            lens = [int(c.shape[0]) for c in codes]
+            T = max(lens)
+            pad = torch.zeros(n, max(T, 1), self.ncg, dtype=torch.long, device=self.dev)
+            for r, c in enumerate(codes):
+                pad[r, :lens[r]] = c
+            self.voc.clear_many(list(range(n)))
+            snaps = [self.voc.snapshot(r) if lens[r] <= 1 else None for r in range(n)]
+            for t in range(T - 1):
+                self.voc.step(pad[:, t], n)
+                for r in range(n):
+                    if lens[r] - 2 == t:
+                        snaps[r] = self.voc.snapshot(r)
+            for r, (key, _) in enumerate(grp):
+                last = codes[r][-1].clone() if lens[r] else self.sil_frame.clone()
+                self.voc_snaps[key] = ([t.cpu().pin_memory() for t in snaps[r]], last.cpu())
+            self.voc.clear_many(list(range(n)))
 
     def _forward_rows(self, x, pos, slot, max_len):
         """Packed causal prefill of rows x [n, H] (bf16, consumed) at positions pos into cache rows slot."""
@@ -477,9 +523,24 @@ class FastEngine:
         self.pf_cpos[:k].copy_(torch.tensor([a + n for a, n in zip(starts, ns)], dtype=torch.int32))
         L.call("a8_prefill_finish", C.byref(self.desc), L.ptr(self.pf_hl), k, L.ptr(self.pf_st), L.ptr(self.pf_cpos),
                L.stream_handle())
-        # codec rows: keep_voc rows keep their state; the others start clean; both decode a silence frame first
-        idx = torch.tensor(slots, dtype=torch.long, device=dev)
-        self.frame_prev.index_copy_(0, idx, self.sil_frame.unsqueeze(0).expand(len(slots), -1).contiguous())
-        fresh = [s for s, r in zip(slots, reqs) if not r.get("keep_voc")]
-        if fresh and self.voc is not None:
-            self.voc.clear_many(fresh)
+        # codec rows (serve/fast_engine.py:1134-1156): keep_voc rows keep their state and decode a silence frame
+        # first; the others start from their voice's primed snapshot (TTS_VOC_PRIME=1) or clean
+        keep, vgroups = [], {}
+        for s, r in zip(slots, reqs):
+            if r.get("keep_voc"):
+                keep.append(s)
+            else:
+                vgroups.setdefault(r["key"] if self.voc_prime else None, []).append(s)
+        if keep:
+            idx = torch.tensor(keep, dtype=torch.long, device=dev)
+            self.frame_prev.index_copy_(0, idx, self.sil_frame.unsqueeze(0).expand(len(keep), -1).contiguous())
+        for key, gslots in vgroups.items():
+            snap = self.voc_snaps.get(key) if key is not None else None
+            idx = torch.tensor(gslots, dtype=torch.long, device=dev)
+            if snap is None:
+                self.voc.clear_many(gslots)
+                first = self.sil_frame
+            else:
+                self.voc.load_many(gslots, snap[0])
+                first = snap[1].to(dev).long()
+            self.frame_prev.index_copy_(0, idx, first.unsqueeze(0).expand(len(gslots), -1).contiguous())

@@ -127,6 +127,34 @@ int a8_tick_start(const int64_t* tok, int64_t* tok_in, int64_t* codes, int ncb, 
 /* y[r] = src[idx[r]] (bf16 rows of H). */
 int a8_gather_rows(const void* src, int lds, const int* idx, void* y, int ldy, int rows, int H, a8_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------- codec */
+/* Channels-last causal conv / polyphase transposed conv as an implicit GEMM, fp16 in, fp32 accumulation
+ * (serve/fast_kernels.py:551-623 conv_cl, serve/fast_engine.py:218-232 _CLConv.__call__):
+ *   y[b, t, n] = bias[n] + sum_{j < taps} sum_c xin[b, t + j*dil, c] * w[n, j*Cin + c]  (+ res[b*res_bs + t*res_ts + n])
+ * xin fp16 [rows, ctx + T, Cin] (Cin a multiple of 32, (taps-1)*dil <= ctx), w fp16 [N, taps*Cin] with N padded to a
+ * multiple of 16 (a transposed conv of stride s: N = s*Cout, n = p*Cout + c, row t holds output rows t*s+p).
+ * mode 0: fp16 y at out[b*out_bs + t*out_ts + n]; mode 1 (conv_out): fp32 tanh(fp16(y[b, t, 0])) at out[b*out_bs + t].
+ * T a power of two (or any T with T % min(T,128) == 0 and 128 % min(T,128) == 0). */
+int a8_conv(const void* xin, int rows, int T, int Cin, int ctx, const void* w, int N, int taps, int dil,
+            const void* bias, const void* res, long long res_bs, long long res_ts, void* out, long long out_bs,
+            long long out_ts, int mode, a8_stream_t stream);
+/* A conv's context-padded input (serve/fast_kernels.py:695-729 snake_cat, serve/fast_engine.py:226-231):
+ * xin[b] = [state[b] (ctx rows) ; fp16(snake(x[b]))], then state[b] = xin[b, T:T+ctx]. x is fp16 (x_bf16 = 0) or
+ * bf16 rows of C at batch stride x_bs elements, state rows state_bs elements apart; snake(v) = v + inv * sin(alpha v)^2 in fp32 (alpha NULL: identity);
+ * ctx = 0: no state. C a multiple of 8. */
+int a8_snake_cat(const void* x, int x_bf16, long long x_bs, int T, int C, void* state, long long state_bs, int ctx,
+                 const float* alpha, const float* inv, void* xin, int rows, a8_stream_t stream);
+/* Upsample stage middle (serve/fast_engine.py:484-489): bf16 causal depthwise conv (K taps <= 8, carried tail
+ * st [rows, K-1, C] at st_bs elements a row, every product and sum rounded to bf16 in tap order, bias first) and LayerNorm(eps) over C
+ * (C a multiple of 128, <= 4096): z = bf16(LN(dwconv([st ; u]))), st = last K-1 input rows. */
+int a8_ups_dwln(const void* u, int T, int C, void* st, long long st_bs, int K, const void* dww, const void* dwb, const void* lnw,
+                const void* lnb, float eps, void* z, int rows, a8_stream_t stream);
+/* Codec input (serve/fast_engine.py:472-477): x[r] = bf16(t_sem[clamp(codes[r,0])] + sum_k t_res[k, clamp(codes[r,k+1])])
+ * (fp32 tables [v_sem, C] and [ncb-1, v_res, C]); pos_c[r] = min(pos[r], max_pos-1), lens[r] = min(pos[r]+1, window),
+ * pos[r] += 1. */
+int a8_codec_embed(const int64_t* codes, int ncb, const float* t_sem, int v_sem, const float* t_res, int v_res, int C,
+                   void* x, int* pos, int* pos_c, int* lens, int max_pos, int window, int rows, a8_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------------- sampling */
 /* out[r] = draw over logits[r, :V] (fp32): top-k (ties: lower index first), top-p on the untempered softmax (the best
  * candidate always kept), temperature, exponential race with E = -log(u), u from Philox4x32-10(key = seed,
@@ -185,6 +213,87 @@ typedef struct A8StackRun {
 /* _Stack.forward (serve/fast_engine.py:117-138): decode rows or packed causal prefill rows. */
 int a8_stack_forward(const A8StackDesc* d, const A8StackRun* r, a8_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------- streaming codec */
+/* One conv of the decoder program: xin = [context ; snake(in)] (a8_snake_cat), out = conv(xin) (+ res) (a8_conv). */
+typedef struct A8ConvOp {
+  const void* w;          /* fp16 [N, taps * Cin] */
+  const void* bias;       /* fp16 [N] or NULL */
+  const float* alpha;     /* snake alpha [Cin] or NULL (no activation) */
+  const float* inv;       /* 1 / (alpha + 1e-9) [Cin] */
+  void* state;            /* fp16 context [slot rows, ctx, Cin] at state_bs elements a row, or NULL (ctx 0) */
+  long long state_bs;
+  int Cin, N, taps, dil, ctx;
+  int T;                  /* input timesteps a frame */
+  int in, out, res;       /* activation buffers act[i]; in -1: the upsample output (bf16); out -1: audio (tanh of
+                             column 0, fp32); res -1: none */
+} A8ConvOp;
+
+/* One upsample stage ([transposed conv k = s = 2 as a GEMM, causal ConvNeXt block], serve/fast_engine.py:479-491). */
+typedef struct A8Upsample {
+  const void* tw;         /* bf16 [2C, C]: rows [0, C) phase 0, [C, 2C) phase 1 */
+  const void* tb;         /* bf16 [2C] */
+  const void* dww;        /* bf16 [K, C] depthwise taps */
+  const void* dwb;        /* bf16 [C] */
+  void* st;               /* bf16 carried tail [slot rows, K - 1, C] at st_bs elements a row */
+  long long st_bs;
+  int K;
+  float eps;
+  const void* lnw;        /* bf16 [C] */
+  const void* lnb;
+  const void* w1;         /* bf16 [mlp, C] */
+  const void* b1;
+  const void* w2;         /* bf16 [C, mlp] */
+  const void* b2;
+  const void* gamma;      /* bf16 [C] */
+  int mlp;
+} A8Upsample;
+
+#define A8_MAX_UPS 4
+#define A8_MAX_CONV_OPS 40
+
+typedef struct A8Vocoder {
+  int B;                  /* slot rows */
+  int ncb, C, v_sem, v_res, max_pos, window, up;
+  const float* t_sem;     /* fp32 [v_sem, C] code table of the semantic codebook (out_proj folded in) */
+  const float* t_res;     /* fp32 [ncb - 1, v_res, C] */
+  int* pos;               /* [B] frames decoded per row */
+  int* pos_c;             /* [B] scratch: this frame's RoPE position */
+  int* lens;              /* [B] scratch: keys attended */
+  void* x;                /* bf16 [B, C] scratch: the transformer's input rows */
+  A8StackDesc post;       /* window transformer (ring = window) */
+  A8Scratch scratch;      /* for B rows */
+  int n_ups;
+  A8Upsample ups[A8_MAX_UPS];
+  void* ubuf[4];          /* bf16 scratch: [B * 2^n_ups, C] x3 and [B * 2^n_ups, mlp] */
+  int n_ops;
+  A8ConvOp ops[A8_MAX_CONV_OPS];
+  void* act[3];           /* fp16 scratch: each the largest [B, T, N] of the program */
+  void* xin;              /* fp16 scratch: the largest [B, ctx + T, Cin] */
+  float* audio;           /* fp32 [B, up] */
+} A8Vocoder;
+
+/* StreamingVocoder.step (serve/fast_engine.py:470-494): one codec frame for rows [0, b): codes [b, ncb] (int64, row
+ * stride ncb) -> audio [b, up]; every row's carried state advances one frame. */
+int a8_voc_step(const A8Vocoder* v, const int64_t* codes, int b, a8_stream_t stream);
+
+/* A piece of per-slot state: for every slot, nchunks chunks of chunk_bytes at base + slot * slot_stride +
+ * k * chunk_stride (addresses and sizes multiples of 4 bytes; 16 for the vector path); in a snapshot it sits at
+ * blob_off (the blob 16-byte aligned). */
+typedef struct A8StateSeg {
+  void* base;
+  long long slot_stride, chunk_bytes, chunk_stride;
+  int nchunks;
+  long long blob_off;
+} A8StateSeg;
+
+enum { A8_STATE_CLEAR = 0, A8_STATE_LOAD = 1, A8_STATE_SNAPSHOT = 2 };
+
+/* The vocoder's row-state arena (serve/fast_engine.py:368-393 _arena_init, :453-468 snapshot / load_many / clear /
+ * clear_many) as one launch over a segment table in device memory: CLEAR zeroes the state of slots[0..nslots),
+ * LOAD copies the snapshot blob into each of them, SNAPSHOT copies slot slots[0] into the blob. */
+int a8_state_rows(const A8StateSeg* segs, int nseg, const int* slots, int nslots, int op, void* blob,
+                  a8_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------------- engine */
 typedef struct A8Engine {
   int B, S, H, ncb, cbk, nsem, vocab, ras_w;
@@ -220,10 +329,14 @@ typedef struct A8Engine {
   const int* f_pos0;      /* int32 [2B]: r % 2 */
   const int* f_slot0;     /* int32 [2B]: r / 2 */
   A8Scratch scratch;      /* for 2B rows */
+  const A8Vocoder* voc;   /* host descriptor of the codec (NULL: the tick makes no audio) */
+  a8_stream_t side;       /* the codec's stream (not the tick's) */
 } A8Engine;
 
 /* One frame for slot rows [0, b): fast AR (2-token pass + ncb - 2 passes, each sampled), slow AR step, semantic
- * draw with RAS, state update. Replaces FastEngine._tick (serve/fast_engine.py:737-769) minus the codec. */
+ * draw with RAS, state update; with a codec, audio[:b] = the codec step of the previous tick's frame_prev, run on the
+ * side stream (forked from and joined back into `stream`). Replaces FastEngine._tick (serve/fast_engine.py:737-769).
+ * The first call with a codec on a device creates the fork / join events: make it outside stream capture. */
 int a8_tick(const A8Engine* e, int b, a8_stream_t stream);
 
 /* The slow AR half of the tick for rows [0, b), reading tok_in and codes as left by the tick's first half: input

@@ -1,0 +1,193 @@
+"""Codec decoder kernels on the GPU, through the C ABI, against the CPU oracle (oracle/ref_cpu.py Conv / Vocoder).
+
+Tolerances: the convs accumulate in fp32 in a different order than the oracle's matmul and round to fp16 once, so an
+output may differ by one fp16 rounding (checked as max relative error <= 4e-3 and >= 95% bit-equal); the carried conv
+context is the activated fp16 input, where fp32 sin() of another library may move a rare value by one fp16 ulp. The
+bf16 op-by-op depthwise conv is the oracle's exact sequence; LayerNorm statistics (fp32, another summation order) may move a result by one bf16 ulp.
+"""
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+from oracle import ref_cpu as R
+
+pytestmark = pytest.mark.gpu
+F16, BF = torch.float16, torch.bfloat16
+
+
+@pytest.fixture(scope="module")
+def L(a8):
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    a8.load()
+    a8._lib.call("a8_clear_error")
+    return a8._lib
+
+
+def rel(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    return float((a - b).abs().max() / b.abs().max().clamp(min=1e-6))
+
+
+def frac_equal(a, b):
+    return float((a.float().cpu() == b.float().cpu()).float().mean())
+
+
+def sync_ok(L):
+    torch.cuda.synchronize()
+    err = L.device_error()
+    assert err[0] == 0, err
+
+
+def make_conv(g, Cin, Cout, k=7, dil=1, trans=False, stride=1, snake=True, Bmax=64):
+    """An oracle Conv over a seeded torch conv module; its context starts random (a stream already running)."""
+    if trans:
+        m = torch.nn.ConvTranspose1d(Cin, Cout, 2 * stride, stride=stride)
+    else:
+        m = torch.nn.Conv1d(Cin, Cout, k, dilation=dil)
+    with torch.no_grad():
+        m.weight.copy_(torch.randn(m.weight.shape, generator=g) * (Cin * m.weight.shape[-1]) ** -0.5)
+        m.bias.copy_(torch.randn(m.bias.shape, generator=g) * 0.1)
+    sm = SimpleNamespace(alpha=torch.rand(1, Cin, 1, generator=g) * 1.5 + 0.2) if snake else None
+    c = R.Conv(SimpleNamespace(conv=m), Bmax, snake_mod=sm, trans=trans)
+    if c.state is not None:
+        c.state.copy_(R.hf(torch.randn(c.state.shape, generator=g)))
+    return c
+
+
+def device_conv(c):
+    """Device weights of an oracle Conv: W2d[p*Cout + co, j*Cin + ci] = W[p, j, ci, co] (fp16), bias, snake terms."""
+    ph, taps, Cin, Cout = c.W.shape
+    w = c.W.permute(0, 3, 1, 2).reshape(ph * Cout, taps * Cin).to(F16).cuda().contiguous()
+    dev = SimpleNamespace(w=w, N=ph * Cout, bias=None, alpha=None, inv=None, state=None)
+    if c.bias is not None:
+        dev.bias = c.bias.repeat(ph).to(F16).cuda()
+    if c.a is not None:
+        dev.alpha, dev.inv = c.a.float().cuda().contiguous(), c.ib.float().cuda().contiguous()
+    if c.state is not None:
+        dev.state = c.state.to(F16).cuda().contiguous()
+    return dev
+
+
+def run_conv(L, c, d, x, b, res=None, mode=0):
+    """snake_cat + conv on the GPU for rows [0, b) of x [b, T, Cin] (fp16 or bf16)."""
+    T = x.shape[1]
+    xin = torch.empty(b, c.ctx + T, c.Cin, dtype=F16, device="cuda")
+    state = d.state[:b] if d.state is not None else None
+    L.call("a8_snake_cat", L.ptr(x), int(x.dtype == BF), T * c.Cin, T, c.Cin, L.ptr(state), c.ctx * c.Cin, c.ctx,
+           L.ptr(d.alpha), L.ptr(d.inv), L.ptr(xin), b, L.stream_handle())
+    if mode == 1:
+        out = torch.empty(b, T, dtype=torch.float32, device="cuda")
+        obs, ots = T, 1
+    else:
+        out = torch.empty(b, T * c.ph, c.Cout, dtype=F16, device="cuda")
+        obs, ots = T * d.N, d.N
+    L.call("a8_conv", L.ptr(xin), b, T, c.Cin, c.ctx, L.ptr(d.w), d.N, c.taps, c.dil, L.ptr(d.bias), L.ptr(res),
+           T * d.N if res is not None else 0, d.N if res is not None else 0, L.ptr(out), obs, ots, mode,
+           L.stream_handle())
+    sync_ok(L)
+    return out
+
+
+CONV_CASES = [
+    # name, Cin, Cout, k, dil, trans, stride, snake, T, rows, in_bf16
+    ("dec_in", 256, 192, 7, 1, False, 1, False, 4, 5, True),
+    ("unit_c1_dil3", 96, 96, 7, 3, False, 1, True, 32, 3, False),
+    ("unit_c1_dil9", 64, 64, 7, 9, False, 1, True, 1024, 2, False),
+    ("trans_s2", 192, 96, 0, 1, True, 2, True, 64, 3, False),
+    ("trans_s8", 256, 128, 0, 1, True, 8, True, 4, 33, False),
+    ("k7_wide", 384, 384, 7, 1, False, 1, True, 256, 2, False),
+]
+
+
+@pytest.mark.parametrize("name,Cin,Cout,k,dil,trans,stride,snake,T,rows,in_bf16", CONV_CASES,
+                         ids=[c[0] for c in CONV_CASES])
+def test_conv_vs_oracle(L, name, Cin, Cout, k, dil, trans, stride, snake, T, rows, in_bf16):
+    g = torch.Generator().manual_seed(Cin * 31 + T + rows)
+    c = make_conv(g, Cin, Cout, k, dil, trans, stride, snake)
+    d = device_conv(c)
+    for step in range(2):                                  # the second step reads the context the first one left
+        xr = torch.randn(rows, T, Cin, generator=g)
+        x = R.bf(xr) if in_bf16 else R.hf(xr)
+        want = c(R.hf(x), rows)
+        got = run_conv(L, c, d, x.to(BF if in_bf16 else F16).cuda(), rows)
+        assert rel(got.view(rows, T * c.ph, c.Cout), want) <= 4e-3, (name, step)
+        assert frac_equal(got.view(rows, T * c.ph, c.Cout), want) >= 0.95, (name, step)
+        st = d.state[:rows].float().cpu()
+        assert frac_equal(st, c.state[:rows]) >= 0.999 and rel(st, c.state[:rows]) <= 1e-3, (name, step)
+
+
+def test_conv_1x1_residual(L):
+    """A residual unit's 1x1 conv: snake on the loads (no context), + bias + the unit's input."""
+    g = torch.Generator().manual_seed(5)
+    c = make_conv(g, 192, 192, k=1, snake=True)
+    d = device_conv(c)
+    rows, T = 2, 256
+    x = R.hf(torch.randn(rows, T, 192, generator=g))
+    res = R.hf(torch.randn(rows, T, 192, generator=g))
+    want = c(x, rows, res=res)
+    got = run_conv(L, c, d, x.to(F16).cuda(), rows, res=res.to(F16).cuda())
+    assert rel(got, want) <= 4e-3 and frac_equal(got, want) >= 0.95
+
+
+def test_conv_out_tanh(L):
+    """conv_out (Cout 1) + tanh into fp32 audio."""
+    g = torch.Generator().manual_seed(6)
+    c = make_conv(g, 96, 1, k=7, snake=True)
+    d = device_conv(c)
+    rows, T = 3, 128
+    for _ in range(2):
+        x = R.hf(torch.randn(rows, T, 96, generator=g))
+        want = torch.tanh(c(x, rows)[..., 0])
+        got = run_conv(L, c, d, x.to(F16).cuda(), rows, mode=1)
+        assert float((got.cpu() - want).abs().max()) <= 2e-3
+
+
+@pytest.mark.parametrize("T,rows", [(2, 3), (4, 5)])
+def test_ups_dwln(L, T, rows):
+    """Upsample stage middle: bf16 7-tap causal depthwise conv with its carried tail, then LayerNorm."""
+    g = torch.Generator().manual_seed(T * 10 + rows)
+    C, K, eps = 1024, 7, 1e-6
+    u = R.bf(torch.randn(rows, T, C, generator=g))
+    st = R.bf(torch.randn(rows, K - 1, C, generator=g))
+    dww, dwb = R.bf(torch.randn(K, C, generator=g) * 0.3), R.bf(torch.randn(C, generator=g) * 0.1)
+    lnw, lnb = R.bf(1 + 0.1 * torch.randn(C, generator=g)), R.bf(0.1 * torch.randn(C, generator=g))
+    xin = torch.cat([st, u], 1)
+    y = R.bf(dwb + R.bf(xin[:, 0:T] * dww[0]))
+    for j in range(1, K):
+        y = R.bf(y + R.bf(xin[:, j:j + T] * dww[j]))
+    want = R.bf(torch.nn.functional.layer_norm(y, (C,), lnw, lnb, eps))
+    want_st = xin[:, T:]
+    ud, std, wd, bd, lwd, lbd = (t.to(BF).cuda().contiguous() for t in (u, st, dww, dwb, lnw, lnb))
+    z = torch.empty(rows, T, C, dtype=BF, device="cuda")
+    L.call("a8_ups_dwln", L.ptr(ud), T, C, L.ptr(std), (K - 1) * C, K, L.ptr(wd), L.ptr(bd), L.ptr(lwd), L.ptr(lbd),
+           eps, L.ptr(z), rows, L.stream_handle())
+    sync_ok(L)
+    assert torch.equal(std.float().cpu(), want_st)
+    assert rel(z, want) <= 1e-2 and frac_equal(z, want) >= 0.97
+
+
+def test_codec_embed(L):
+    """Code tables with the codec's clamps, and the window transformer's positions."""
+    g = torch.Generator().manual_seed(7)
+    C, vs, vr, ncb, rows = 1024, 4096, 1024, 10, 6
+    t_sem = torch.randn(vs, C, generator=g)
+    t_res = torch.randn(ncb - 1, vr, C, generator=g)
+    codes = torch.randint(0, 4096, (rows, ncb), generator=g)
+    codes[0, 0], codes[1, 3], codes[2, 9], codes[3, 0] = -5, 4000, -1, 5000      # out of range: clamped
+    voc = SimpleNamespace(t_sem=t_sem, t_res=t_res, v_sem=vs, v_res=vr)
+    want = R.bf(R.Vocoder.embed(voc, codes))
+    pos = torch.tensor([0, 5, 127, 128, 8191, 9000], dtype=torch.int32)
+    max_pos, win = 8192, 128
+    pd = pos.cuda()
+    pos_c, lens = torch.empty_like(pd), torch.empty_like(pd)
+    x = torch.empty(rows, C, dtype=BF, device="cuda")
+    cd, sd, rd = codes.cuda(), t_sem.cuda(), t_res.cuda()
+    L.call("a8_codec_embed", L.ptr(cd), ncb, L.ptr(sd), vs, L.ptr(rd), vr, C, L.ptr(x),
+           L.ptr(pd), L.ptr(pos_c), L.ptr(lens), max_pos, win, rows, L.stream_handle())
+    sync_ok(L)
+    assert rel(x, want) <= 1e-2 and frac_equal(x, want) >= 0.99
+    assert torch.equal(pos_c.cpu(), pos.clamp(max=max_pos - 1))
+    assert torch.equal(lens.cpu(), (pos + 1).clamp(max=win))
+    assert torch.equal(pd.cpu(), pos + 1)

@@ -217,24 +217,46 @@ def test_engine_ticks_match_oracle(a8, dev, tiny_model, do_sample):
 
 
 def test_engine_graph_replay_equals_eager(a8, dev, tiny_model):
-    """A captured tick graph replays exactly what the eager launches compute."""
+    """A captured tick graph (codec on its side stream included) replays exactly what the eager launches compute."""
     gp = dict(do_sample=True, temperature=0.8, top_k=50, top_p=0.95)
     eng = a8.FastEngine(tiny_model, StubTokenizer(), gp, max_slots=4, max_seq=512, buckets=[2, 4],
                         seq_from_env=False, seed=5)
     eng.capture(log=lambda *a: None)
     reqs = _requests(1)
     eng.admit([0, 1], reqs)
-    snap = [t.clone() for t in (eng.tok, eng.hid, eng.cpos, eng.prev, eng.nstep, eng.tick_ctr, eng.frame_prev,
-                                 eng.slow.kc, eng.slow.vc)]
+    state = [eng.tok, eng.hid, eng.cpos, eng.prev, eng.nstep, eng.tick_ctr, eng.frame_prev, eng.slow.kc,
+             eng.slow.vc] + [s[0] for s in eng.voc._states()]
+    snap = [t.clone() for t in state]
     outs = []
     for _ in range(3):
         eng.replay(2)
-        outs.append((eng.tok_in[:2].clone(), eng.frame_prev[:2].clone(), eng.tok[:2].clone()))
-    for t, s in zip((eng.tok, eng.hid, eng.cpos, eng.prev, eng.nstep, eng.tick_ctr, eng.frame_prev, eng.slow.kc,
-                     eng.slow.vc), snap):
+        outs.append((eng.tok_in[:2].clone(), eng.frame_prev[:2].clone(), eng.tok[:2].clone(), eng.audio[:2].clone()))
+    for t, s in zip(state, snap):
         t.copy_(s)
     for i in range(3):
         eng.tick(2)
         assert torch.equal(eng.tok_in[:2], outs[i][0]) and torch.equal(eng.frame_prev[:2], outs[i][1])
-        assert torch.equal(eng.tok[:2], outs[i][2])
+        assert torch.equal(eng.tok[:2], outs[i][2]) and torch.equal(eng.audio[:2], outs[i][3])
+    assert a8.device_error()[0] == 0
+
+
+def test_engine_tick_audio_is_codec_of_previous_frame(a8, dev, tiny_model):
+    """Each tick's audio is the codec step of the frame the previous tick chose (frame_prev as the tick starts):
+    bit-identical to a standalone StreamingVocoder fed those frames -- the side stream reads frame_prev before the
+    tick's draw rewrites it. A fresh row's first frame is the silence frame."""
+    from audio8_b200.codec import StreamingVocoder
+    gp = dict(do_sample=True, temperature=0.8, top_k=50, top_p=0.95)
+    eng = a8.FastEngine(tiny_model, StubTokenizer(), gp, max_slots=3, max_seq=512, buckets=[3],
+                        seq_from_env=False, seed=9)
+    voc = StreamingVocoder(tiny_model.load_codec(device="cpu"), 3, dev)
+    reqs = _requests(2)
+    reqs.append(dict(reqs[0], text="11 22 33 44"))
+    eng.admit([0, 1, 2], reqs)
+    assert torch.equal(eng.frame_prev[:3].cpu(), eng.sil_frame.cpu().expand(3, -1))
+    for t in range(4):
+        fp = eng.frame_prev[:3].clone()
+        eng.tick(3)
+        want = voc.step(fp, 3)
+        torch.cuda.synchronize()
+        assert torch.equal(eng.audio[:3], want), t
     assert a8.device_error()[0] == 0
