@@ -131,6 +131,8 @@ def cpu_sample(steps, threads=None):
 
 
 def run_reference(args):
+    if args.workload == "cfg2":
+        return run_reference_cfg2(args)
     value, cores, dt = cpu_sample(max(1, args.steps))
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": 0, "ms_per_step": round(1000 * dt / max(1, args.steps), 3),
@@ -138,6 +140,20 @@ def run_reference(args):
             "data": "synthetic", "config": cfg_dict(1),
             "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port",
                              "sample": f"{args.steps} cfg1 steps (64 rows, KV U[200,1500], 24 layers + head)"},
+            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_cfg2(args):
+    steps = max(1, min(args.steps, 2))
+    value, cores, dt = cpu_sample_cfg2(args.cpu_rows, steps)
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
+            "steps": steps, "warmup": 0, "ms_per_step": round(1000 * dt / steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (bf16 / fp16 rounding points)", "data": "synthetic",
+            "config": cfg2_dict(1),
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": f"{steps} cfg2 tick(s) of {args.cpu_rows} of the 192 rows (full tick with "
+                                       f"codec) on the CPU restatement"},
             "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -335,14 +351,231 @@ def roofline(eng, L, lens, dev, args):
                        for k, v in cand.items() if k != name}}
 
 
+# ---------------------------------------------------------------------------------------------------- cfg2
+B_CFG2 = 192
+L2_LO, L2_HI = 100, 2000
+
+
+def cfg2_lengths(b=B_CFG2):
+    import torch
+    g = torch.Generator().manual_seed(2)
+    return torch.randint(L2_LO, L2_HI + 1, (b,), generator=g)
+
+
+def cfg2_dict(world):
+    return {"workload": "cfg2: full tick, bf16, 192 rows: fast AR (2-token pass + 8 passes), slow AR step (KV length "
+                        "U[100,2000], seed 2), streaming codec (window-128 transformer, 2 upsample stages, 29-conv "
+                        "decoder, 2048 samples a row) on its side stream; codes uniform random",
+            "model": "Audio8 stand-in (seeded random weights, reference shapes)", "global_batch": B_CFG2 * world,
+            "seq_len": f"{L2_LO}-{L2_HI}", "parallelism": f"replicas x{world}",
+            "l2": "inputs larger than L2 (~0.9 GB of weights + ~1.5 GB of slow KV read a tick)"}
+
+
+def cpu_sample_cfg2(rows, ticks, threads=None):
+    """The CPU restatement of the cfg2 tick (all host threads) on `rows` of the 192: frames/s."""
+    import torch
+    from oracle import ref_cpu as R
+    from oracle.standin import StandinConfig, StubTokenizer, build_standin
+    torch.set_num_threads(threads or os.cpu_count())
+    m = build_standin(0, StandinConfig())
+    gp = dict(do_sample=True, temperature=0.8, top_k=50, top_p=0.95)
+    ora = R.OracleEngine(m, StubTokenizer(), gp, max_slots=rows, max_seq=2048, seed=1234)
+    del m
+    lens = cfg2_lengths()[:rows]
+    g = torch.Generator().manual_seed(3)
+    for t in (ora.slow.kc, ora.slow.vc):
+        t[:, :rows].copy_(R.bf(torch.randn(t[:, :rows].shape, generator=g)))
+    ora.cpos[:rows] = (lens - 1).to(torch.int32)
+    ora.tok[:rows] = ora.sb + torch.randint(0, 4096, (rows,), generator=g)
+    ora.hid[:rows] = R.bf(torch.randn(rows, ora.H, generator=g))
+    ora.frame_prev[:rows] = torch.randint(0, 4096, (rows, ora.ncg), generator=g)
+    ora.nstep[:rows] = 5
+    t0 = time.perf_counter()
+    for _ in range(ticks):
+        ora.cpos[:rows] = (lens - 1).to(torch.int32)
+        ora.tick(rows)
+    dt = time.perf_counter() - t0
+    return rows * ticks / dt, torch.get_num_threads(), dt
+
+
+def conv_flops(voc, b):
+    """Algorithmic FLOPs of each decoder conv of one codec step at b rows (output channels unpadded)."""
+    out = []
+    for c, T, *_ in voc.ops:
+        out.append(2 * b * T * (c.ph * c.Cout) * c.taps * c.Cin)
+    return out
+
+
+def run_ours_cfg2(args, rank, world, local):
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__ as G
+    from oracle.standin import StandinConfig, StubTokenizer, build_standin
+    G.build()
+    a8 = G.load_package()
+    L = a8._lib
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    model = build_standin(0, StandinConfig())
+    gp = dict(do_sample=True, temperature=0.8, top_k=50, top_p=0.95)
+    b = B_CFG2
+    eng = a8.FastEngine(model, StubTokenizer(), gp, max_slots=b, max_seq=2048, buckets=[b], seq_from_env=False,
+                        seed=1234 + rank)
+    del model
+    lens = cfg2_lengths()
+    g = torch.Generator(device=dev).manual_seed(3 + rank)
+    for t in (eng.slow.kc, eng.slow.vc, eng.voc.post.kc, eng.voc.post.vc):
+        t.normal_(generator=g)
+    eng.voc.pos.fill_(1000)                               # steady state: every row attends a full 128-frame window
+    cpos0 = (lens - 1).to(torch.int32).to(dev)
+    eng.cpos[:b].copy_(cpos0)
+    tok0 = (eng.sb + torch.randint(0, 4096, (b,), generator=g, device=dev)).long()
+    frame0 = torch.randint(0, 4096, (b, eng.ncg), generator=g, device=dev)
+    eng.tok[:b].copy_(tok0)
+    eng.frame_prev.copy_(frame0)
+    eng.hid[:b].normal_(generator=g)
+    eng.nstep[:b].fill_(5)
+
+    def step():
+        eng.cpos[:b].copy_(cpos0)
+        eng.tick(b)
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    n0 = L.load().a8_launch_count()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    launches = L.load().a8_launch_count() - n0
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.barrier()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t)
+    value = world * b * args.steps / (ms / 1000.0)
+    err = a8.device_error()
+    assert err[0] == 0, err
+
+    # end to end as the serving loop drives it: each tick's input state (tokens, the frame to decode) from pinned host
+    # memory, then the tick, then its audio, consumed tokens and frames read back
+    h_tok, h_frame = tok0.cpu().pin_memory(), frame0.cpu().pin_memory()
+    h_audio = torch.empty(b, eng.up, dtype=torch.float32).pin_memory()
+    h_tin = torch.empty(b, dtype=torch.int64).pin_memory()
+    h_fp = torch.empty(b, eng.ncg, dtype=torch.int64).pin_memory()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record()
+    for _ in range(args.steps):
+        eng.tok[:b].copy_(h_tok, non_blocking=True)
+        eng.frame_prev.copy_(h_frame, non_blocking=True)
+        graph.replay()
+        h_audio.copy_(eng.audio[:b], non_blocking=True)
+        h_tin.copy_(eng.tok_in[:b], non_blocking=True)
+        h_fp.copy_(eng.frame_prev[:b], non_blocking=True)
+    e3.record()
+    torch.cuda.synchronize()
+    ms_e2e = e2.elapsed_time(e3)
+    t = torch.tensor([ms_e2e], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_e2e = float(t)
+    e2e = {"value": round(world * b * args.steps / (ms_e2e / 1000.0), 3), "unit": UNIT,
+           "h2d_bytes_per_step": h_tok.numel() * 8 + h_frame.numel() * 8,
+           "d2h_bytes_per_step": h_audio.numel() * 4 + h_tin.numel() * 8 + h_fp.numel() * 8}
+    del graph
+    roof, convs = conv_roofline(eng, L, dev, b, args)
+    line = None
+    if rank == 0:
+        tick_ms = ms / args.steps
+        line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(tick_ms, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (codec convs fp16)", "data": "synthetic",
+                "config": cfg2_dict(world), "roofline": roof, "e2e": e2e, "gpu_launches": int(launches) * args.steps,
+                "clocks": clk.summary(),
+                "realtime": {"frame_ms": round(1000 * eng.up / eng.sr, 3), "rtf_at_192": round(
+                    tick_ms / (1000 * eng.up / eng.sr), 4)},
+                "codec_convs": convs}
+        if world == 1 and not args.no_cpu:
+            rows = args.cpu_rows
+            v, cores, dt = cpu_sample_cfg2(rows, args.cpu_steps)
+            line["cpu_baseline"] = {"value": round(v, 3), "unit": UNIT, "cores": cores, "kind": "port",
+                                    "sample": f"{args.cpu_steps} cfg2 tick(s) of {rows} of the 192 rows on the CPU "
+                                              f"oracle ({dt:.1f} s)"}
+    if world > 1:
+        dist.barrier()
+    return line
+
+
+def conv_roofline(eng, L, dev, b, args):
+    """Each decoder conv of the codec step timed alone (CUDA events around each launch on its stream, L2 flushed
+    between launches); the roofline line is the conv with the largest total time (tensor-bound: its algorithmic
+    FLOPs / duration against the measured bf16 peak; fp16 and bf16 run at the same tensor-core rate)."""
+    import torch
+    _, tf, kind = _peaks()
+    voc = eng.voc
+    flops = conv_flops(voc, b)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    reps = max(3, min(10, args.steps))
+    res = []
+    for i, (c, T, src, dst, rr) in enumerate(voc.ops):
+        out, obs, ots, mode = (voc.audio, voc.up, 1, 1) if dst < 0 else (voc.act[dst], T * c.N, c.N, 0)
+        r = voc.act[rr] if rr >= 0 else None
+        args_ = (L.ptr(voc.xin), b, T, c.Cin, c.ctx, L.ptr(c.w), c.N, c.taps, c.dil, L.ptr(c.bias), L.ptr(r),
+                 T * c.N if r is not None else 0, c.N if r is not None else 0, L.ptr(out), obs, ots, mode)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps + 2)]
+        for k, (a, z) in enumerate(ev):
+            flush.zero_()
+            a.record()
+            L.call("a8_conv", *args_, L.stream_handle())
+            z.record()
+        torch.cuda.synchronize()
+        t = sum(a.elapsed_time(z) for a, z in ev[2:]) / reps / 1000.0
+        res.append({"op": i, "Cin": c.Cin, "N": c.N, "taps": c.taps, "T": T, "us": round(t * 1e6, 2),
+                    "tflops": round(flops[i] / t / 1e12, 1)})
+    assert L.device_error()[0] == 0
+    top = max(res, key=lambda x: x["us"])
+    achieved = flops[top["op"]] / (top["us"] * 1e-6) / 1e12
+    total_us = sum(x["us"] for x in res)
+    roof = {"kernel": f"k_conv (decoder op {top['op']}: Cin {top['Cin']}, N {top['N']}, taps {top['taps']}, "
+                      f"T {top['T']}, {b} rows)", "bound": "tensor", "achieved": round(achieved, 1), "peak": tf,
+            "unit": "TFLOP/s", "frac": round(achieved / tf, 4), "peak_kind": f"{kind} (burst bf16)",
+            "traffic": None, "algorithmic_flops_per_launch": flops[top["op"]], "us_per_launch": top["us"],
+            "all_convs": {"us_total": round(total_us, 1), "tflops": round(sum(flops) / (total_us * 1e-6) / 1e12, 1)}}
+    return roof, res
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="cfg1", choices=["cfg1"])
-    ap.add_argument("--cpu-steps", type=int, default=3)
+    ap.add_argument("--workload", default="cfg2", choices=["cfg1", "cfg2"])
+    ap.add_argument("--cpu-steps", type=int, default=None, help="CPU baseline sample: steps (cfg1 3, cfg2 2)")
+    ap.add_argument("--cpu-rows", type=int, default=64, help="cfg2 CPU baseline sample: rows of the 192")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -350,6 +583,8 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     args.gpus = world if world > 1 else args.gpus
+    if args.cpu_steps is None:
+        args.cpu_steps = 3 if args.workload == "cfg1" else 2
     if args.impl == "reference":
         if rank == 0:
             run_reference(args)
@@ -361,7 +596,7 @@ def main():
         import torch.distributed as dist
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
-    line = run_ours(args, rank, world, local)
+    line = (run_ours if args.workload == "cfg1" else run_ours_cfg2)(args, rank, world, local)
     if rank == 0 and line is not None:
         print(json.dumps(line), flush=True)
     if world > 1:
