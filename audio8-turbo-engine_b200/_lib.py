@@ -49,10 +49,22 @@ MAX_UPS, MAX_CONV_OPS = 4, 40
 STATE_CLEAR, STATE_LOAD, STATE_SNAPSHOT = 0, 1, 2
 
 
+class A8ConvRun(C.Structure):
+    _fields_ = [("xin", c_void_p), ("rows", c_int), ("T", c_int), ("Cin", c_int), ("ctx", c_int), ("w", c_void_p),
+                ("N", c_int), ("taps", c_int), ("dil", c_int), ("bias", c_void_p), ("res", c_void_p),
+                ("res_bs", c_ll), ("res_ts", c_ll), ("raw", c_void_p), ("raw_bs", c_ll), ("raw_ts", c_ll),
+                ("nxt", c_void_p), ("nxt_bs", c_ll), ("nxt_off", c_ll), ("cout", c_int), ("alpha", c_void_p),
+                ("inv", c_void_p), ("audio", c_void_p), ("audio_bs", c_ll)]
+
+
+class A8CtxShift(C.Structure):
+    _fields_ = [("xin", c_void_p), ("ctx", c_int), ("T", c_int), ("Cin", c_int)]
+
+
 class A8ConvOp(C.Structure):
-    _fields_ = [("w", c_void_p), ("bias", c_void_p), ("alpha", c_void_p), ("inv", c_void_p), ("state", c_void_p),
-                ("state_bs", c_ll), ("Cin", c_int), ("N", c_int), ("taps", c_int), ("dil", c_int), ("ctx", c_int),
-                ("T", c_int), ("in_", c_int), ("out", c_int), ("res", c_int)]
+    _fields_ = [("w", c_void_p), ("bias", c_void_p), ("alpha", c_void_p), ("inv", c_void_p), ("xin", c_void_p),
+                ("Cin", c_int), ("N", c_int), ("taps", c_int), ("dil", c_int), ("ctx", c_int), ("T", c_int),
+                ("raw", c_int), ("res", c_int)]
 
 
 class A8Upsample(C.Structure):
@@ -67,8 +79,8 @@ class A8Vocoder(C.Structure):
                 ("window", c_int), ("up", c_int), ("t_sem", c_void_p), ("t_res", c_void_p), ("pos", c_void_p),
                 ("pos_c", c_void_p), ("lens", c_void_p), ("x", c_void_p), ("post", A8StackDesc),
                 ("scratch", A8Scratch), ("n_ups", c_int), ("ups", A8Upsample * MAX_UPS), ("ubuf", c_void_p * 4),
-                ("n_ops", c_int), ("ops", A8ConvOp * MAX_CONV_OPS), ("act", c_void_p * 3), ("xin", c_void_p),
-                ("audio", c_void_p)]
+                ("n_ops", c_int), ("ops", A8ConvOp * MAX_CONV_OPS), ("act", c_void_p * 2), ("ctx_table", c_void_p),
+                ("n_ctx", c_int), ("conv_ctas", c_int), ("audio", c_void_p)]
 
 
 class A8StateSeg(C.Structure):
@@ -113,15 +125,16 @@ SIGNATURES = {
     "a8_gather_rows": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "a8_sample": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_float, c_float, c_ull, c_int, c_void_p,
                           c_void_p, c_void_p]),
-    "a8_conv": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
-                        c_ll, c_ll, c_void_p, c_ll, c_ll, c_int, c_void_p]),
-    "a8_snake_cat": (c_int, [c_void_p, c_int, c_ll, c_int, c_int, c_void_p, c_ll, c_int, c_void_p, c_void_p,
-                             c_void_p, c_int, c_void_p]),
+    "a8_conv": (c_int, [C.POINTER(A8ConvRun), c_void_p]),
+    "a8_ctx_shift": (c_int, [c_void_p, c_int, c_int, c_void_p]),
+    "a8_conv_input": (c_int, [c_void_p, c_int, c_ll, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int,
+                              c_void_p]),
     "a8_ups_dwln": (c_int, [c_void_p, c_int, c_int, c_void_p, c_ll, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
                             c_float, c_void_p, c_int, c_void_p]),
     "a8_codec_embed": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p,
                                c_void_p, c_int, c_int, c_int, c_void_p]),
     "a8_voc_step": (c_int, [C.POINTER(A8Vocoder), c_void_p, c_int, c_void_p]),
+    "a8_voc_decode": (c_int, [C.POINTER(A8Vocoder), c_void_p, c_int, c_void_p]),
     "a8_state_rows": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "a8_stack_forward": (c_int, [C.POINTER(A8StackDesc), C.POINTER(A8StackRun), c_void_p]),
     "a8_tick": (c_int, [C.POINTER(A8Engine), c_int, c_void_p]),

@@ -4,12 +4,15 @@ serve/fast_engine.py:312-494, same constructor, ``step``, ``snapshot`` / ``load_
 The step is ONE C-ABI call (``a8_voc_step``) over an ``A8Vocoder`` descriptor built here: code tables, the window-128
 transformer (a ``PackedStack`` with a 128-entry ring cache), two upsample stages (GEMMs + depthwise conv / LayerNorm
 kernel), then the decoder as a program of implicit-GEMM convs (fp16 channels-last, fp32 tensor-core accumulation).
-A row's carried state (conv contexts, upsample tails, ring KV, frame count) is listed in a segment table so that
-clearing, loading or snapshotting a row is one kernel (``a8_state_rows``).
+Each conv owns its input rows ``xin`` [B, ctx + T, Cin]: rows [0, ctx) are its carried (activated) context, the rest
+is written by the previous conv's epilogue, already activated with this conv's snake; one kernel at the end of the
+step moves every context forward a frame. A row's carried state (conv contexts, upsample tails, ring KV, frame count)
+is listed in a segment table so that clearing, loading or snapshotting a row is one kernel (``a8_state_rows``).
 """
 from __future__ import annotations
 
 import ctypes as C
+import os
 from typing import List
 
 import torch
@@ -44,12 +47,13 @@ class _Conv:
         self.Cin, self.Cout = Cin, Cout
         self.N = self.ph * Cout
         self.w = W.permute(0, 3, 1, 2).reshape(self.N, self.taps * Cin).to(F16).to(dev).contiguous()
-        self.bias = c.bias.detach().float().cpu().repeat(self.ph).to(F16).to(dev) if c.bias is not None else None
+        self.bias = c.bias.detach().float().cpu().repeat(self.ph).to(F16).float().to(dev) \
+            if c.bias is not None else None                       # the fp16 bias, held as fp32
         self.alpha = self.inv = None
         if snake_mod is not None:
             al = snake_mod.alpha.detach().float().cpu().reshape(-1)
             self.alpha, self.inv = al.to(dev).contiguous(), (1.0 / (al + 1e-9)).to(dev).contiguous()
-        self.state = torch.zeros(Bmax, self.ctx, Cin, dtype=F16, device=dev) if self.ctx > 0 else None
+        self.T, self.xin = 0, None                  # input timesteps a frame and input rows: set by the program
 
 
 class StreamingVocoder:
@@ -119,28 +123,32 @@ class StreamingVocoder:
             self.blocks.append((tc, units))
         self.final = _Conv(mods[6], B, dev, snake_mod=mods[5])
         self.ops = self._program(Tup)
-        act = max(op[0].N * op[1] for op in self.ops)
-        xin = max((op[0].ctx + op[1]) * op[0].Cin for op in self.ops)
-        self.act = [torch.zeros(B * act, dtype=F16, device=dev) for _ in range(3)]
-        self.xin = torch.zeros(B * xin, dtype=F16, device=dev)
+        for c, T, *_ in self.ops:                        # each conv's input rows, its carried context first
+            c.T = T
+            c.xin = torch.zeros(B, c.ctx + T, c.Cin, dtype=F16, device=dev)
+        act = max([c.N * T for c, T, raw, _ in self.ops if raw >= 0] + [16])
+        self.act = [torch.zeros(B * act, dtype=F16, device=dev) for _ in range(2)]
         self.audio = torch.zeros(B, self.up, dtype=F32, device=dev)
+        ctx = [L.A8CtxShift(xin=c.xin.data_ptr(), ctx=c.ctx, T=c.T, Cin=c.Cin) for c in self.convs() if c.ctx > 0]
+        raw = bytes((L.A8CtxShift * len(ctx))(*ctx))
+        self.ctx_table = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(dev)
+        self.n_ctx = len(ctx)
         self.desc = self._describe()
         self._arena_init()
 
     # ---- the descriptor ----
     def _program(self, T):
-        """[(conv, T_in, in, out, res)]: buffers 0..2 rotate; in -1 = the upsample output, out -1 = audio."""
-        ops = [(self.dec_in, T, -1, 0, -1)]
-        cur = 0
+        """[(conv, T_in, raw, res)]: raw = the act buffer (0 / 1) that keeps the conv's raw output for a later
+        residual (a unit's input), res = the buffer added to its output (the unit's input, at the unit's 1x1 conv)."""
+        ops = [(self.dec_in, T, -1, -1)]
         for tc, units in self.blocks:
-            nxt = (cur + 1) % 3
-            ops.append((tc, T, cur, nxt, -1))
-            cur, T = nxt, T * tc.ph
-            for c1, c2 in units:
-                tmp, other = [i for i in range(3) if i != cur]
-                ops += [(c1, T, cur, tmp, -1), (c2, T, tmp, other, cur)]
-                cur = other
-        ops.append((self.final, T, cur, -1, -1))
+            ops.append((tc, T, 0, -1))
+            T, cur = T * tc.ph, 0
+            for k, (c1, c2) in enumerate(units):
+                keep = 1 - cur if k + 1 < len(units) else -1
+                ops += [(c1, T, -1, -1), (c2, T, keep, cur)]
+                cur = 1 - cur
+        ops.append((self.final, T, -1, -1))
         assert T == self.up, T
         return ops
 
@@ -162,21 +170,39 @@ class StreamingVocoder:
         for i, t in enumerate(self.ubuf):
             d.ubuf[i] = t.data_ptr()
         d.n_ops = len(self.ops)
-        for i, (c, T, src, dst, res) in enumerate(self.ops):
+        for i, (c, T, raw, res) in enumerate(self.ops):
             o = d.ops[i]
             o.w, o.bias, o.alpha, o.inv = L.ptr(c.w), L.ptr(c.bias), L.ptr(c.alpha), L.ptr(c.inv)
-            o.state = L.ptr(c.state)
-            o.state_bs = c.ctx * c.Cin
+            o.xin = L.ptr(c.xin)
             o.Cin, o.N, o.taps, o.dil, o.ctx, o.T = c.Cin, c.N, c.taps, c.dil, c.ctx, T
-            o.in_, o.out, o.res = src, dst, res
+            o.raw, o.res = raw, res
         for i, t in enumerate(self.act):
             d.act[i] = t.data_ptr()
-        d.xin, d.audio = L.ptr(self.xin), L.ptr(self.audio)
+        d.ctx_table, d.n_ctx = L.ptr(self.ctx_table), self.n_ctx
+        d.conv_ctas = int(os.environ.get("A8_CONV_CTAS", "0"))
+        d.audio = L.ptr(self.audio)
         return d
 
     def convs(self):
         """Every decoder conv, in order (serve/fast_engine.py:394-404, without the tuning metadata)."""
         return [op[0] for op in self.ops]
+
+    def conv_run(self, i, b):
+        """The a8_conv launch of program op i at b rows, as a8_voc_step makes it (to time one conv alone)."""
+        c, T, raw, res = self.ops[i]
+        r = L.A8ConvRun(xin=L.ptr(c.xin), rows=b, T=T, Cin=c.Cin, ctx=c.ctx, w=L.ptr(c.w), N=c.N, taps=c.taps,
+                        dil=c.dil, bias=L.ptr(c.bias))
+        if res >= 0:
+            r.res, r.res_bs, r.res_ts = self.act[res].data_ptr(), T * c.N, c.N
+        if raw >= 0:
+            r.raw, r.raw_bs, r.raw_ts = self.act[raw].data_ptr(), T * c.N, c.N
+        if i + 1 < len(self.ops):
+            nx = self.ops[i + 1][0]
+            r.nxt, r.nxt_bs, r.nxt_off, r.cout = nx.xin.data_ptr(), (nx.ctx + nx.T) * nx.Cin, nx.ctx * nx.Cin, nx.Cin
+            r.alpha, r.inv = L.ptr(nx.alpha), L.ptr(nx.inv)
+        else:
+            r.audio, r.audio_bs = self.audio.data_ptr(), self.up
+        return r
 
     def tune(self, b, log=print, cache_path=None):
         """The reference tunes Triton tile configs per conv; these kernels size their tiles from the shapes."""
@@ -187,9 +213,8 @@ class StreamingVocoder:
         """(tensor, chunks a slot, chunk elements, chunk stride elements, slot stride elements) of every state."""
         out = []
         for c in self.convs():
-            if c.state is not None:
-                n = c.state[0].numel()
-                out.append((c.state, 1, n, n, n))
+            if c.ctx > 0:                               # the context rows at the head of each slot's input rows
+                out.append((c.xin, 1, c.ctx * c.Cin, 0, c.xin[0].numel()))
         for u in self.ups:
             n = u["st"][0].numel()
             out.append((u["st"], 1, n, n, n))
@@ -247,4 +272,10 @@ class StreamingVocoder:
         codes = codes.contiguous()
         assert codes.dtype == torch.int64 and codes.shape[1] == self.ncb
         L.call("a8_voc_step", C.byref(self.desc), L.ptr(codes), int(b), L.stream_handle())
+        return self.audio[:b]
+
+    def decode(self, u, b):
+        """The conv decoder alone (serve/fast_engine.py:301-309): u [b, 4, C] bf16 -> audio [b, 2048] fp32."""
+        u = u.to(BF16).contiguous()
+        L.call("a8_voc_decode", C.byref(self.desc), L.ptr(u), int(b), L.stream_handle())
         return self.audio[:b]

@@ -1,8 +1,8 @@
 // Memory-bound kernels of the streaming codec decoder (serve/fast_engine.py:312-494, StreamingVocoder.step):
 //   k_codec_embed   codes -> code-table sum (fp32) -> bf16 transformer input; the window transformer's positions
-//   k_snake_cat     a conv's context-padded input: [carried activated context ; snake(x)], context carried forward
+//   k_conv_input    a conv's input rows (after its carried context) from a tensor, activated or copied
 //   k_ups_dwln      upsample stage: causal 7-tap depthwise conv with carried tail + LayerNorm (bf16 op by op)
-// All are PDL secondaries; one block per batch row keeps each row's carried state update inside one block.
+// All are PDL secondaries; a batch row's carried state is updated inside one block.
 #include "common.cuh"
 
 namespace a8 {
@@ -62,44 +62,33 @@ __device__ __forceinline__ void load8(const __nv_bfloat16* p, float* v) {
   }
 }
 
-// xin[b] = concat(state[b] (ctx rows, activated), snake(x[b]) (T rows)); then state[b] = xin[b, T:T+ctx]
-// (serve/fast_kernels.py:695-729 and serve/fast_engine.py:226-231). snake(v) = v + inv * sin(alpha v)^2 in fp32,
-// stored fp16; alpha == null: plain fp16 copy. One block per batch row.
+// A conv's input rows from a tensor: xin[b, ctx + t, c] = fp16(act(x[b, t, c])), act(v) = v + inv * sin(alpha v)^2
+// in fp32 (serve/fast_kernels.py:695-729 snake_cat; the context rows [0, ctx) already hold the carried context);
+// alpha == null: plain fp16 copy. grid (rows, parts): part p of batch row b, 8 channels a thread.
 template <typename TIn>
-__global__ void k_snake_cat(const TIn* __restrict__ x, long long x_bs, int T, int C, __half* state, long long s_bs, int ctx,
-                            const float* __restrict__ alpha, const float* __restrict__ inv, __half* __restrict__ xin,
-                            int rows) {
+__global__ void k_conv_input(const TIn* __restrict__ x, long long x_bs, int T, int C, __half* __restrict__ xin,
+                             int ctx, const float* __restrict__ alpha, const float* __restrict__ inv, int rows) {
   pdl_launch();
   pdl_wait();
   const int b = blockIdx.x;
   if (b >= rows) return;
-  __half* xb = xin + (size_t)b * (ctx + T) * C;
-  __half* sb = state != nullptr ? state + (size_t)b * s_bs : nullptr;
+  __half* xb = xin + ((size_t)b * (ctx + T) + ctx) * C;
   const TIn* src = x + (size_t)b * x_bs;
-  const int total = (ctx + T) * C;
-  for (int idx = threadIdx.x * 8; idx < total; idx += blockDim.x * 8) {
-    const int row = idx / C, c = idx % C;              // C is a multiple of 8: the 8 channels share a row
-    uint4 out;
-    if (row < ctx) {
-      out = *reinterpret_cast<const uint4*>(sb + (size_t)row * C + c);
-    } else {
-      float v[8];
-      load8(src + (size_t)(row - ctx) * C + c, v);
-      if (alpha != nullptr) {
+  const int total = T * C;
+  for (int idx = (blockIdx.y * blockDim.x + threadIdx.x) * 8; idx < total; idx += gridDim.y * blockDim.x * 8) {
+    const int c = idx % C;                             // C is a multiple of 8: the 8 channels share a row
+    float v[8];
+    load8(src + idx, v);
+    if (alpha != nullptr) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float s = sinf(v[i] * alpha[c + i]);
-          v[i] = v[i] + inv[c + i] * s * s;
-        }
+      for (int i = 0; i < 8; ++i) {
+        const float s = sinf(v[i] * alpha[c + i]);
+        v[i] = v[i] + inv[c + i] * s * s;
       }
-      out = make_uint4(pack_f16(v[0], v[1]), pack_f16(v[2], v[3]), pack_f16(v[4], v[5]), pack_f16(v[6], v[7]));
     }
-    *reinterpret_cast<uint4*>(xb + (size_t)row * C + c) = out;
+    *reinterpret_cast<uint4*>(xb + idx) =
+        make_uint4(pack_f16(v[0], v[1]), pack_f16(v[2], v[3]), pack_f16(v[4], v[5]), pack_f16(v[6], v[7]));
   }
-  if (sb == nullptr) return;
-  __syncthreads();                                     // this block's xin rows are written (and visible to it)
-  for (int idx = threadIdx.x * 8; idx < ctx * C; idx += blockDim.x * 8)
-    *reinterpret_cast<uint4*>(sb + idx) = *reinterpret_cast<const uint4*>(xb + (size_t)T * C + idx);
 }
 
 // Upsample stage tail (serve/fast_engine.py:484-489): y[t] = dwb + sum_j xin[t + j] * w[j] with a bf16 rounding after
@@ -165,9 +154,9 @@ __global__ void k_ups_dwln(const __nv_bfloat16* __restrict__ u, int T, int C, __
     for (int k = 0; k < 4; ++k) sb[(size_t)i * C + c0 + k] = __float2bfloat16_rn(nt[i][k]);
 }
 
-static cudaError_t launch_rows(const void* fn, int rows, int threads, void** args, cudaStream_t s) {
+static cudaError_t launch_rows(const void* fn, int rows, int threads, void** args, cudaStream_t s, int parts = 1) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(rows);
+  cfg.gridDim = dim3(rows, parts);
   cfg.blockDim = dim3(threads);
   cfg.stream = s;
   cudaLaunchAttribute at[1];
@@ -186,24 +175,26 @@ int codec_embed(const int64_t* codes, int ncb, const float* t_sem, int v_sem, co
   return launch_rows((const void*)k_codec_embed, rows, 256, args, s) == cudaSuccess ? A8_OK : A8_ERR_CUDA;
 }
 
-int snake_cat(const void* x, int x_bf16, long long x_bs, int T, int C, void* state, long long s_bs, int ctx, const float* alpha,
-              const float* inv, void* xin, int rows, cudaStream_t s) {
-  if (C % 8) return A8_ERR_ARG;
-  __half* sp = reinterpret_cast<__half*>(state);
+int conv_input(const void* x, int x_bf16, long long x_bs, int T, int C, void* xin, int ctx, const float* alpha,
+               const float* inv, int rows, cudaStream_t s) {
+  if (C % 8 || x_bs % 8) return A8_ERR_ARG;
   __half* xp = reinterpret_cast<__half*>(xin);
+  const int parts = std::max(1, std::min(64, (T * C / 8 + 255) / 256));
   if (x_bf16) {
     const __nv_bfloat16* xs = reinterpret_cast<const __nv_bfloat16*>(x);
-    void* args[] = {&xs, &x_bs, &T, &C, &sp, &s_bs, &ctx, &alpha, &inv, &xp, &rows};
-    return launch_rows((const void*)k_snake_cat<__nv_bfloat16>, rows, 256, args, s) == cudaSuccess ? A8_OK
-                                                                                                   : A8_ERR_CUDA;
+    void* args[] = {&xs, &x_bs, &T, &C, &xp, &ctx, &alpha, &inv, &rows};
+    return launch_rows((const void*)k_conv_input<__nv_bfloat16>, rows, 256, args, s, parts) == cudaSuccess
+               ? A8_OK
+               : A8_ERR_CUDA;
   }
   const __half* xs = reinterpret_cast<const __half*>(x);
-  void* args[] = {&xs, &x_bs, &T, &C, &sp, &s_bs, &ctx, &alpha, &inv, &xp, &rows};
-  return launch_rows((const void*)k_snake_cat<__half>, rows, 256, args, s) == cudaSuccess ? A8_OK : A8_ERR_CUDA;
+  void* args[] = {&xs, &x_bs, &T, &C, &xp, &ctx, &alpha, &inv, &rows};
+  return launch_rows((const void*)k_conv_input<__half>, rows, 256, args, s, parts) == cudaSuccess ? A8_OK
+                                                                                                   : A8_ERR_CUDA;
 }
 
-int ups_dwln(const void* u, int T, int C, void* st, long long st_bs, int K, const void* dww, const void* dwb, const void* lnw,
-             const void* lnb, float eps, void* z, int rows, cudaStream_t s) {
+int ups_dwln(const void* u, int T, int C, void* st, long long st_bs, int K, const void* dww, const void* dwb,
+             const void* lnw, const void* lnb, float eps, void* z, int rows, cudaStream_t s) {
   if (C % 128 || C > 4096 || K > 8) return A8_ERR_ARG;
   const __nv_bfloat16* up = reinterpret_cast<const __nv_bfloat16*>(u);
   __nv_bfloat16* sp = reinterpret_cast<__nv_bfloat16*>(st);
@@ -218,10 +209,11 @@ int ups_dwln(const void* u, int T, int C, void* st, long long st_bs, int K, cons
 
 using namespace a8;
 
-extern "C" int a8_snake_cat(const void* x, int x_bf16, long long x_bs, int T, int C, void* state, long long state_bs, int ctx,
-                            const float* alpha, const float* inv, void* xin, int rows, a8_stream_t stream) {
-  if (x == nullptr || xin == nullptr || rows <= 0 || T <= 0 || (ctx > 0 && state == nullptr)) return A8_ERR_ARG;
-  return snake_cat(x, x_bf16, x_bs, T, C, state, state_bs, ctx, alpha, inv, xin, rows, reinterpret_cast<cudaStream_t>(stream));
+extern "C" int a8_conv_input(const void* x, int x_bf16, long long x_bs, int T, int C, void* xin, int ctx,
+                             const float* alpha, const float* inv, int rows, a8_stream_t stream) {
+  if (x == nullptr || xin == nullptr || rows <= 0 || T <= 0 || ctx < 0 || (alpha != nullptr && inv == nullptr))
+    return A8_ERR_ARG;
+  return conv_input(x, x_bf16, x_bs, T, C, xin, ctx, alpha, inv, rows, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int a8_ups_dwln(const void* u, int T, int C, void* st, long long st_bs, int K, const void* dww, const void* dwb,

@@ -1,40 +1,153 @@
-// Channels-last causal convolution / polyphase transposed convolution of the codec's conv decoder as a tcgen05
-// implicit GEMM (serve/fast_kernels.py:551-623 conv_cl; serve/fast_engine.py:178-232 _CLConv).
+// Channels-last causal convolution / polyphase transposed convolution of the codec's conv decoder as a persistent,
+// warp-specialized tcgen05 implicit GEMM (serve/fast_kernels.py:551-623 conv_cl, :695-729 snake_cat;
+// serve/fast_engine.py:178-232 _CLConv).
 //
-//   out[b, t, n] = epi( sum_j sum_c xin[b, t + j*dil, c] * W[n, j*Cin + c] ),   t in [0, T)
+//   y[b, t, n] = bias[n] + sum_j sum_c xin[b, t + j*dil, c] * W[n, j*Cin + c]  (+ res[b, t, n]),   t in [0, T)
 //
-// xin is the context-padded input [rows, ctx + T, Cin] (fp16, the left context first). A transposed conv (stride s,
-// kernel 2s, right crop s) is a 2-tap conv whose N = s * Cout holds every phase (n = p * Cout + c), so row (b, t) of
-// the result is already output rows t*s .. t*s+s-1 of [rows, T*s, Cout].
+// xin is the conv's input [rows, ctx + T, Cin] (fp16) with its carried context in rows [0, ctx). A transposed conv
+// (stride s, kernel 2s, right crop s) is a 2-tap conv whose N = s * Cout holds every phase (n = p * Cout + c), so row
+// (b, t) of y is output timesteps t*s .. t*s+s-1 of [rows, T*s, Cout].
 //
-// One CTA = 128 token rows (TB batch rows x TT timesteps) x ntile output channels. The A tile of K block (tap j,
-// channel block c) is ONE 3-D TMA box {KC, TT, TB} at (c*KC, t0 + j*dil, b0) of xin viewed as [rows][ctx+T][Cin] --
-// the tap shift is just a coordinate. B = weight tile {KC, ntile}. fp16 x fp16 -> fp32 accumulator in TMEM
-// (tcgen05.mma kind::f16), a TMA ring of stages, one producer lane, one MMA lane, four epilogue warps (thread = token
-// row, tcgen05.ld 32 channels at a time): + bias, + residual, fp16 store; or tanh into fp32 audio (conv_out).
+// Work unit = 128 token rows (TB batch rows x TT timesteps) x ntile output channels. The A tile of K block (tap j,
+// channel block c) is ONE 3-D TMA box {KC, TT, TB} at (c*KC, t0 + j*dil, b0) of xin -- the tap shift is a coordinate.
+// One CTA per SM loops over work units:
+//   warp 0      TMA producer: a ring of `stages` A+B slots
+//   warp 1      MMA issuer (tcgen05.mma kind::f16, fp16 x fp16 -> fp32) into one of two TMEM accumulators
+//   warps 2-9   epilogue: while the MMA fills one accumulator, these drain the other (tcgen05.ld 16 columns at a time;
+//               a lane quarter of TMEM is shared by two warps, which split the columns)
+// The epilogue writes, per output: the raw fp16 y (the residual stream), and/or the NEXT conv's input rows
+// snake(y) (x + inv * sin(alpha x)^2 on the fp16 y, stored fp16) straight into that conv's xin after its context --
+// so no separate activation pass -- or, for conv_out, tanh(fp16 y) into fp32 audio.
 #include "common.cuh"
 
 namespace a8 {
 
 constexpr int KERNEL_ID_CONV = 4;
+constexpr int CONV_EPI_WARPS = 16;
+constexpr int CONV_THREADS = 64 + 32 * CONV_EPI_WARPS;
 
 struct ConvArgs {
   int rows, T, Cin, N, taps, dil, ctx;
-  int KC;                 // channels per K block: 64 (128-byte swizzle) or 32 (64-byte swizzle)
-  int TT, TB;             // token tile: TB batch rows x TT timesteps (TT * TB == 128)
-  int ntile, n_tiles;
+  int KC;                   // channels per K block: 64 (128-byte swizzle) or 32 (64-byte swizzle)
+  int TT, TB;               // token tile: TB batch rows x TT timesteps (TT * TB == 128)
+  int ntile, n_tiles, m_tiles;
   int kb_total, stages;
-  uint32_t tmem_cols;
-  const __half* bias;     // [N] or null
-  const __half* res;      // residual, same indexing as out (fp16) or null
+  uint32_t acc_cols;        // TMEM columns of one accumulator (power of two >= ntile)
+  const float* bias;        // [N] (fp16 values as fp32) or null
+  const __half* res;        // [b*res_bs + t*res_ts + n] or null
   long long res_bs, res_ts;
-  void* out;
-  long long out_bs, out_ts;   // element strides of a batch row and of a timestep row
-  int mode;               // 0: fp16 out; 1: tanh of column 0 into fp32 out[b * out_bs + t]
+  __half* raw;              // [b*raw_bs + t*raw_ts + n] or null
+  long long raw_bs, raw_ts;
+  __half* nxt;              // [b*nxt_bs + nxt_off + t*N + n] or null: the next conv's input rows
+  long long nxt_bs, nxt_off;
+  int cout;                 // channels of an output timestep (N / phases): the activation's channel is n % cout
+  const float* alpha;       // [cout] activation of nxt, or null (identity)
+  const float* inv;
+  float* audio;             // tanh mode: audio[b*audio_bs + t] = tanh(fp16(y[b, t, 0])), or null
+  long long audio_bs;
 };
 
+// 32 lanes x 16 consecutive 32-bit columns
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// fp32 <-> fp16 on the IEEE-754 fields with integer arithmetic, so the epilogue's many conversions run on the integer
+// pipes instead of the conversion unit. to_f16: round to nearest even, returning the fp16 bits and (in r) the
+// rounded value as fp32; exact for results in the fp16 normal range below 2^15 (|v| in [2^-14, 32768)), the
+// conversion instruction for everything else (zero, subnormal, large, inf, nan).
+__device__ __forceinline__ uint32_t to_f16(float v, float& r) {
+  const uint32_t u = __float_as_uint(v);
+  const uint32_t e = (u >> 23) & 0xFFu;
+  if (e - 113u <= 28u) {                             // biased fp32 exponent 113..141
+    const uint32_t q = (u + 0xFFFu + ((u >> 13) & 1u)) & 0xFFFFE000u;
+    r = __uint_as_float(q);
+    return ((q >> 16) & 0x8000u) | ((((q >> 23) & 0xFFu) - 112u) << 10) | ((q >> 13) & 0x3FFu);
+  }
+  const __half h = __float2half_rn(v);
+  r = __half2float(h);
+  return __half_as_ushort(h);
+}
+// Branch-free forms of the two conversions for the epilogue's hot path: valid for fp16 normal numbers (and, for
+// f32_to_f16_fast, results below 2^15); `ok` is cleared for any other input, and the caller redoes such a chunk with
+// the exact conversions. f32_to_f16_fast rounds v to nearest even in place and returns the fp16 bits.
+__device__ __forceinline__ uint32_t f32_to_f16_fast(float& v, bool& ok) {
+  const uint32_t u = __float_as_uint(v);
+  ok &= ((u >> 23) & 0xFFu) - 113u <= 28u;
+  const uint32_t q = (u + 0xFFFu + ((u >> 13) & 1u)) & 0xFFFFE000u;
+  v = __uint_as_float(q);
+  return ((q >> 16) & 0x8000u) | ((((q >> 23) & 0xFFu) - 112u) << 10) | ((q >> 13) & 0x3FFu);
+}
+__device__ __forceinline__ float f16_to_f32_fast(uint32_t h, bool& ok) {
+  const uint32_t e = (h >> 10) & 0x1Fu;
+  ok &= e - 1u < 30u;
+  return __uint_as_float(((h & 0x8000u) << 16) | ((e + 112u) << 23) | ((h & 0x3FFu) << 13));
+}
+
+// sin^2(t) for |t| < 2^15 without branches: t = k pi/2 + r with k = rint(2t/pi) (round-to-nearest by adding 1.5 2^23)
+// and r = t - k pi/2 by a two-term split of pi/2 (Cody-Waite reduction with fused multiply-adds); then
+// sin^2(r) = r^2 P(r^2) with P the Taylor series of (sin r / r)^2 = sum_n (-1)^n 2^(2n+1) r^(2n) / (2n+2)!, which for
+// |r| <= pi/4 is within 1e-10 after seven terms; odd k swaps sin^2 for cos^2 = 1 - sin^2.
+__device__ __forceinline__ float sin2_reduced(float t) {
+  const float big = fmaf(t, 0.636619772367581343f, 12582912.0f);
+  const float k = big - 12582912.0f;
+  const uint32_t odd = __float_as_uint(big) & 1u;
+  float r = fmaf(-k, 1.57079637050628662109375f, t);     // pi/2 rounded to fp32
+  r = fmaf(-k, -4.37113900018624283e-8f, r);             // pi/2 minus that
+  const float u = r * r;
+  float p = 9.39683970e-8f;                              // 2^13 / 14!
+  p = fmaf(p, u, -4.27556185e-6f);                       // -2^11 / 12!
+  p = fmaf(p, u, 1.41093474e-4f);                        // 2^9 / 10!
+  p = fmaf(p, u, -3.17460317e-3f);                       // -2^7 / 8!
+  p = fmaf(p, u, 4.44444444e-2f);                        // 2^5 / 6!
+  p = fmaf(p, u, -3.33333333e-1f);                       // -2^3 / 4!
+  p = fmaf(p, u, 1.0f);                                  // 2 / 2!
+  const float s2 = u * p;
+  return odd ? 1.0f - s2 : s2;
+}
+
+// fp16 bits -> fp32 (exact): normal numbers and zeros by field arithmetic, the rest by the conversion instruction
+__device__ __forceinline__ float from_f16(uint32_t h) {
+  const uint32_t e = (h >> 10) & 0x1Fu;
+  if (e - 1u < 30u) return __uint_as_float(((h & 0x8000u) << 16) | ((e + 112u) << 23) | ((h & 0x3FFu) << 13));
+  if ((h & 0x7FFFu) == 0) return __uint_as_float((h & 0x8000u) << 16);
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(h)));
+}
+
+// The epilogue of one 16-column chunk with the exact conversions and sinf, from the raw accumulators v: fp16 y into
+// hy and, with an activation, fp16 act(y) into ha (two values a word).
+__device__ __forceinline__ void exact_chunk(const ConvArgs& a, const float* v, int b, int t, int nb, bool act,
+                                            uint32_t* hy, uint32_t* ha) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int n = nb + i;
+    float x = v[i];
+    if (a.bias != nullptr) x += a.bias[n];
+    if (a.res != nullptr) x += __half2float(a.res[(size_t)b * a.res_bs + (size_t)t * a.res_ts + n]);
+    const __half h = __float2half_rn(x);
+    const float y = __half2float(h);
+    const uint32_t hb = __half_as_ushort(h);
+    hy[i / 2] = (i & 1) ? (hy[i / 2] & 0xFFFFu) | (hb << 16) : hb;
+    if (act) {
+      const int c = n % a.cout;
+      const float s = sinf(y * a.alpha[c]);
+      const uint32_t hz = __half_as_ushort(__float2half_rn(y + a.inv[c] * s * s));
+      ha[i / 2] = (i & 1) ? (ha[i / 2] & 0xFFFFu) | (hz << 16) : hz;
+    }
+  }
+}
+
 template <int KC>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(CONV_THREADS, 1)
     k_conv(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, const ConvArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -43,15 +156,19 @@ __global__ void __launch_bounds__(128, 1)
   const uint32_t stage_bytes = a_bytes + b_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * stage_bytes);
   uint64_t* empty = full + stages;
-  uint64_t* accum = empty + stages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* tfull = empty + stages;       // [2] accumulator ready
+  uint64_t* tempty = tfull + 2;           // [2] accumulator drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  // the epilogue's per-column constants, staged once: bias [N], then alpha and inv [cout] (no global loads per tile)
+  float* s_bias = reinterpret_cast<float*>(smem + stages * stage_bytes + 256);
+  float* s_alpha = s_bias + (a.bias != nullptr ? (a.N + 3) / 4 * 4 : 0);
+  float* s_inv = s_alpha + (a.cout + 3) / 4 * 4;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tiles_t = a.T / a.TT;
-  const int mt = blockIdx.x;                      // token tile: (batch group, time block)
-  const int b0 = (mt / tiles_t) * a.TB, t0 = (mt % tiles_t) * a.TT;
-  const int n0 = blockIdx.y * a.ntile;
   const int cblocks = a.Cin / KC;
+  const int nkb = a.kb_total;
+  const int total = a.m_tiles * a.n_tiles;
 
   if (tid == 0) {
     tma_prefetch(&tmX);
@@ -60,10 +177,13 @@ __global__ void __launch_bounds__(128, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], CONV_EPI_WARPS);
+    }
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, a.tmem_cols);
+  if (warp == 1) tmem_alloc(tmem_slot, 2 * a.acc_cols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -72,118 +192,251 @@ __global__ void __launch_bounds__(128, 1)
 
   auto tileA = [&](int s) { return smem + s * stage_bytes; };
   auto tileB = [&](int s) { return smem + s * stage_bytes + a_bytes; };
-  const int nkb = a.kb_total;
+  auto coords = [&](int tile, int* b0, int* t0, int* n0) {
+    const int mt = tile / a.n_tiles, nt = tile % a.n_tiles;
+    *b0 = (mt / tiles_t) * a.TB;
+    *t0 = (mt % tiles_t) * a.TT;
+    *n0 = nt * a.ntile;
+  };
+
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_last(), pol_x = policy_evict_first();
-      const int pre = min(stages, nkb);
-      for (int i = 0; i < pre; ++i) {           // weights do not depend on the previous kernel
-        mbar_arrive_expect_tx(&full[i], stage_bytes);
-        const int j = i / cblocks, c = i % cblocks;
-        tma_load_2d(tileB(i), &tmW, &full[i], j * a.Cin + c * KC, n0, pol_w);
+      // the first tile's weights do not depend on the previous kernel: start them before waiting for it
+      const int first = blockIdx.x;
+      int q = 0;                             // k blocks issued so far (all tiles)
+      bool ok = true;
+      if (first < total) {
+        int b0, t0, n0;
+        coords(first, &b0, &t0, &n0);
+        const int pre = min(stages, nkb);
+        for (int i = 0; i < pre; ++i) {
+          mbar_arrive_expect_tx(&full[i], stage_bytes);
+          tma_load_2d(tileB(i), &tmW, &full[i], (i / cblocks) * a.Cin + (i % cblocks) * KC, n0, pol_w);
+        }
+        pdl_wait();
+        for (int i = 0; i < pre; ++i)
+          tma_load_3d(tileA(i), &tmX, &full[i], (i % cblocks) * KC, t0 + (i / cblocks) * a.dil, b0, pol_x);
+        q = pre;
+        for (int i = pre; i < nkb; ++i) {
+          const int s = i % stages;
+          if (!(ok = mbar_wait(&empty[s], ((i / stages) & 1) ^ 1, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
+          mbar_arrive_expect_tx(&full[s], stage_bytes);
+          tma_load_2d(tileB(s), &tmW, &full[s], (i / cblocks) * a.Cin + (i % cblocks) * KC, n0, pol_w);
+          tma_load_3d(tileA(s), &tmX, &full[s], (i % cblocks) * KC, t0 + (i / cblocks) * a.dil, b0, pol_x);
+          q = i + 1;
+        }
+      } else {
+        pdl_wait();
       }
-      pdl_wait();
-      for (int i = 0; i < pre; ++i) {
-        const int j = i / cblocks, c = i % cblocks;
-        tma_load_3d(tileA(i), &tmX, &full[i], c * KC, t0 + j * a.dil, b0, pol_x);
+      for (int tile = first + gridDim.x; tile < total && ok; tile += gridDim.x) {
+        int b0, t0, n0;
+        coords(tile, &b0, &t0, &n0);
+        for (int i = 0; i < nkb; ++i, ++q) {
+          const int s = q % stages;
+          if (!(ok = mbar_wait(&empty[s], ((q / stages) & 1) ^ 1, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
+          mbar_arrive_expect_tx(&full[s], stage_bytes);
+          tma_load_2d(tileB(s), &tmW, &full[s], (i / cblocks) * a.Cin + (i % cblocks) * KC, n0, pol_w);
+          tma_load_3d(tileA(s), &tmX, &full[s], (i % cblocks) * KC, t0 + (i / cblocks) * a.dil, b0, pol_x);
+        }
       }
-      int issued = pre;
-      for (int i = pre; i < nkb; ++i) {
-        const int s = i % stages;
-        if (!mbar_wait(&empty[s], ((i / stages) - 1) & 1, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV)) break;
-        const int j = i / cblocks, c = i % cblocks;
-        mbar_arrive_expect_tx(&full[s], stage_bytes);
-        tma_load_2d(tileB(s), &tmW, &full[s], j * a.Cin + c * KC, n0, pol_w);
-        tma_load_3d(tileA(s), &tmX, &full[s], c * KC, t0 + j * a.dil, b0, pol_x);
-        issued = i + 1;
-      }
-      for (int i = max(0, issued - stages); i < issued; ++i)
+      // every load issued has landed before the CTA can exit (also after a timeout)
+      for (int i = max(0, q - stages); i < q; ++i)
         mbar_wait(&full[i % stages], (i / stages) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = umma_idesc(128, a.ntile, 0);   // fp16 x fp16 -> fp32
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % stages;
-        if (!mbar_wait(&full[s], (i / stages) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV)) break;
+      int q = 0, it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
+        const int acc = it & 1, use = it >> 1;
+        if (!(ok = mbar_wait(&tempty[acc], (use & 1) ^ 1, ERR_TIMEOUT_ACCUM, KERNEL_ID_CONV))) break;
         tc_fence_after();
-        uint64_t da, db;
-        if constexpr (KC == 64) {
-          da = umma_desc_sw128(tileA(s));
-          db = umma_desc_sw128(tileB(s));
-        } else {
-          da = umma_desc_sw64(tileA(s));
-          db = umma_desc_sw64(tileB(s));
-        }
+        const uint32_t d = tmem + acc * a.acc_cols;
+        for (int i = 0; i < nkb; ++i, ++q) {
+          const int s = q % stages;
+          if (!(ok = mbar_wait(&full[s], (q / stages) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
+          tc_fence_after();
+          uint64_t da, db;
+          if constexpr (KC == 64) {
+            da = umma_desc_sw128(tileA(s));
+            db = umma_desc_sw128(tileB(s));
+          } else {
+            da = umma_desc_sw64(tileA(s));
+            db = umma_desc_sw64(tileB(s));
+          }
 #pragma unroll
-        for (int k = 0; k < KC / 16; ++k) umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (i | k) != 0);
-        umma_commit(&empty[s]);
+          for (int k = 0; k < KC / 16; ++k) umma_f16(d, da + 2 * k, db + 2 * k, idesc, (i | k) != 0);
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&tfull[acc]);             // (after a timeout too: the epilogue is not left waiting)
       }
-      umma_commit(accum);
-    }
-  }
-  __syncwarp();
-  pdl_wait();
-  const bool ok = mbar_wait(accum, 0, ERR_TIMEOUT_ACCUM, KERNEL_ID_CONV);
-  __syncthreads();
-  tc_fence_after();
-
-  // epilogue: thread = token row
-  const int r = warp * 32 + lane;
-  const int b = b0 + r / a.TT, t = t0 + r % a.TT;
-  const bool live = b < a.rows;
-  const uint32_t trow = tmem + (uint32_t(warp * 32) << 16);
-  if (a.mode == 1) {
-    float v[32];
-    tmem_ld32(trow, v);
-    if (live && ok) {
-      const float bias = a.bias != nullptr ? __half2float(a.bias[0]) : 0.f;
-      reinterpret_cast<float*>(a.out)[(size_t)b * a.out_bs + t] = tanhf(f16r(v[0] + bias));
     }
   } else {
-    const int nch = (min(a.ntile, a.N - n0) + 31) / 32;
-    for (int ch = 0; ch < (a.ntile + 31) / 32; ++ch) {
-      float v[32];
-      tmem_ld32(trow + ch * 32, v);
-      if (!live || ch >= nch) continue;
-      const int nb = n0 + ch * 32;
-      const int nn = min(32, a.N - nb);
-      float o[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        float x = ok ? v[i] : 0.f;
-        if (a.bias != nullptr && i < nn) x += __half2float(a.bias[nb + i]);
-        o[i] = x;
-      }
-      if (a.res != nullptr) {
-        const __half* rp = a.res + (size_t)b * a.res_bs + (size_t)t * a.res_ts + nb;
-        if (nn == 32) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint4 u = reinterpret_cast<const uint4*>(rp)[q];
-            const float2 x0 = unpack_f16(u.x), x1 = unpack_f16(u.y), x2 = unpack_f16(u.z), x3 = unpack_f16(u.w);
-            o[8 * q] += x0.x; o[8 * q + 1] += x0.y; o[8 * q + 2] += x1.x; o[8 * q + 3] += x1.y;
-            o[8 * q + 4] += x2.x; o[8 * q + 5] += x2.y; o[8 * q + 6] += x3.x; o[8 * q + 7] += x3.y;
+    // ---------------------------------------------------------------- epilogue warps
+    const int ew = warp - 2;                  // 0 .. CONV_EPI_WARPS-1
+    const int quarter = warp & 3;             // TMEM lanes [32 quarter, +32) are this warp's
+    const int part = ew >> 2;                 // the warps on one quarter split the 16-column chunks round robin
+    constexpr int PARTS = CONV_EPI_WARPS / 4;
+    const int r = quarter * 32 + lane;        // token row of the tile
+    {                                         // weights, not written by the previous kernel: before its end
+      const int et = tid - 64;
+      if (a.bias != nullptr)
+        for (int i = et; i < a.N; i += 32 * CONV_EPI_WARPS) s_bias[i] = a.bias[i];
+      if (a.alpha != nullptr)
+        for (int i = et; i < a.cout; i += 32 * CONV_EPI_WARPS) {
+          s_alpha[i] = a.alpha[i];
+          s_inv[i] = a.inv[i];
+        }
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * CONV_EPI_WARPS) : "memory");   // the epilogue warps only
+    }
+    pdl_wait();                               // outputs may be buffers the previous kernel still reads
+    const int nchunk = (a.ntile + 15) / 16;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+      const int acc = it & 1, use = it >> 1;
+      const bool ok = mbar_wait(&tfull[acc], use & 1, ERR_TIMEOUT_ACCUM, KERNEL_ID_CONV);
+      if (!ok) break;                         // (recorded; the MMA has stopped too)
+      tc_fence_after();
+      int b0, t0, n0;
+      coords(tile, &b0, &t0, &n0);
+      const int b = b0 + r / a.TT, t = t0 + r % a.TT;
+      const bool live = b < a.rows;
+      const uint32_t trow = tmem + acc * a.acc_cols + (uint32_t(quarter * 32) << 16);
+      if (a.audio != nullptr) {
+        if (part == 0) {
+          float v[16];
+          tmem_ld16(trow, v);
+          if (live) {
+            const float bias = a.bias != nullptr ? a.bias[0] : 0.f;
+            float y;
+            to_f16(v[0] + bias, y);
+            a.audio[(size_t)b * a.audio_bs + t] = tanhf(y);
           }
-        } else {
-          for (int i = 0; i < nn; ++i) o[i] += __half2float(rp[i]);
+        }
+      } else {
+        for (int ch = part; ch < nchunk; ch += PARTS) {
+          const int nb = n0 + ch * 16;
+          if (nb >= a.N) break;                // warp-uniform
+          float v[16];
+          tmem_ld16(trow + ch * 16, v);
+          const int nn = min(16, a.N - nb);
+          if (nn == 16) {
+            // straight-line fast path (no branches, so the 16 columns interleave); a chunk where any value leaves
+            // the fast path's range is redone exactly below (warp-uniform)
+            bool ok = true;
+            const bool act = a.nxt != nullptr && a.alpha != nullptr;
+            uint32_t hy[8], ha[8];
+            if (a.bias != nullptr) {
+#pragma unroll
+              for (int i = 0; i < 16; i += 4) {
+                const float4 bv = *reinterpret_cast<const float4*>(s_bias + nb + i);
+                v[i] += bv.x;
+                v[i + 1] += bv.y;
+                v[i + 2] += bv.z;
+                v[i + 3] += bv.w;
+              }
+            }
+            if (a.res != nullptr && live) {
+              const uint4* rp = reinterpret_cast<const uint4*>(a.res + (size_t)b * a.res_bs + (size_t)t * a.res_ts + nb);
+              const uint4 r0 = rp[0], r1 = rp[1];
+              const uint32_t w[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                v[2 * i] += f16_to_f32_fast(w[i] & 0xFFFFu, ok);
+                v[2 * i + 1] += f16_to_f32_fast(w[i] >> 16, ok);
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {                    // v becomes the fp16 y (as fp32)
+              const uint32_t lo = f32_to_f16_fast(v[2 * i], ok), hi = f32_to_f16_fast(v[2 * i + 1], ok);
+              hy[i] = lo | (hi << 16);
+            }
+            if (act) {
+              const int c = nb % a.cout;
+#pragma unroll
+              for (int i = 0; i < 16; i += 4) {
+                const float4 al = *reinterpret_cast<const float4*>(s_alpha + c + i);
+                const float4 iv = *reinterpret_cast<const float4*>(s_inv + c + i);
+                const float al4[4] = {al.x, al.y, al.z, al.w}, iv4[4] = {iv.x, iv.y, iv.z, iv.w};
+                uint32_t h[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  const float tt = v[i + k] * al4[k];
+                  ok &= fabsf(tt) < 32768.f;
+                  float y = fmaf(iv4[k], sin2_reduced(tt), v[i + k]);
+                  h[k] = f32_to_f16_fast(y, ok);
+                }
+                ha[i / 2] = h[0] | (h[1] << 16);
+                ha[i / 2 + 1] = h[2] | (h[3] << 16);
+              }
+            }
+            if (!__all_sync(0xffffffffu, ok || !live)) {   // rare: zeros, subnormals, huge values
+              tmem_ld16(trow + ch * 16, v);
+              if (live) exact_chunk(a, v, b, t, nb, act, hy, ha);
+            }
+            if (live) {
+              if (a.raw != nullptr) {
+                uint4* d = reinterpret_cast<uint4*>(a.raw + (size_t)b * a.raw_bs + (size_t)t * a.raw_ts + nb);
+                d[0] = make_uint4(hy[0], hy[1], hy[2], hy[3]);
+                d[1] = make_uint4(hy[4], hy[5], hy[6], hy[7]);
+              }
+              if (a.nxt != nullptr) {
+                const uint32_t* o = act ? ha : hy;
+                uint4* d = reinterpret_cast<uint4*>(a.nxt + (size_t)b * a.nxt_bs + a.nxt_off + (size_t)t * a.N + nb);
+                d[0] = make_uint4(o[0], o[1], o[2], o[3]);
+                d[1] = make_uint4(o[4], o[5], o[6], o[7]);
+              }
+            }
+          } else if (live) {
+            for (int i = 0; i < nn; ++i) {
+              const int n = nb + i;
+              float x = v[i];
+              if (a.bias != nullptr) x += a.bias[n];
+              if (a.res != nullptr) x += __half2float(a.res[(size_t)b * a.res_bs + (size_t)t * a.res_ts + n]);
+              x = f16r(x);
+              if (a.raw != nullptr) a.raw[(size_t)b * a.raw_bs + (size_t)t * a.raw_ts + n] = __float2half_rn(x);
+              if (a.nxt != nullptr) {
+                if (a.alpha != nullptr) {
+                  const int c = n % a.cout;
+                  const float s = sinf(x * a.alpha[c]);
+                  x = x + a.inv[c] * s * s;
+                }
+                a.nxt[(size_t)b * a.nxt_bs + a.nxt_off + (size_t)t * a.N + n] = __float2half_rn(x);
+              }
+            }
+          }
         }
       }
-      __half* op = reinterpret_cast<__half*>(a.out) + (size_t)b * a.out_bs + (size_t)t * a.out_ts + nb;
-      if (nn == 32) {
-        uint4* d4 = reinterpret_cast<uint4*>(op);
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          d4[q] = make_uint4(pack_f16(o[8 * q], o[8 * q + 1]), pack_f16(o[8 * q + 2], o[8 * q + 3]),
-                             pack_f16(o[8 * q + 4], o[8 * q + 5]), pack_f16(o[8 * q + 6], o[8 * q + 7]));
-      } else {
-        for (int i = 0; i < nn; ++i) op[i] = __float2half_rn(o[i]);
-      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, a.tmem_cols);
+  if (warp == 1) tmem_dealloc(tmem, 2 * a.acc_cols);
+}
+
+// ------------------------------------------------------------------------------------------------ context shift
+// After a codec step: every conv's carried context becomes the last ctx rows its input had, xin[b, :ctx] =
+// xin[b, T : T + ctx] (serve/fast_engine.py:230-231 state update). Rows move in chunks of T so a chunk never
+// overlaps its source (ctx > T: the old context's tail moves down first). One block per (conv, batch row).
+__global__ void k_ctx_shift(const A8CtxShift* __restrict__ tab, int rows) {
+  pdl_launch();
+  pdl_wait();
+  const A8CtxShift e = tab[blockIdx.x];
+  const int b = blockIdx.y;
+  if (b >= rows) return;
+  uint4* base = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(e.xin) + (size_t)b * (e.ctx + e.T) * e.Cin);
+  const int vec_row = e.Cin / 8;
+  for (int r0 = 0; r0 < e.ctx; r0 += e.T) {
+    const int nrow = min(e.T, e.ctx - r0);
+    for (int i = threadIdx.x; i < nrow * vec_row; i += blockDim.x)
+      base[(size_t)r0 * vec_row + i] = base[(size_t)(r0 + e.T) * vec_row + i];
+    __syncthreads();
+  }
 }
 
 // ------------------------------------------------------------------------------------------------ host
@@ -194,15 +447,14 @@ struct ConvPlan {
   int smem;
 };
 
-// xin: fp16 [rows, ctx + T, Cin]; w: fp16 [N, taps * Cin] (K-major)
-int conv_plan(ConvPlan* p, const void* xin, int rows, int T, int Cin, int ctx, const void* w, int N, int taps, int dil,
-              const void* bias, const void* res, long long res_bs, long long res_ts, void* out, long long out_bs,
-              long long out_ts, int mode) {
-  if (xin == nullptr || w == nullptr || out == nullptr || rows <= 0 || T <= 0 || Cin <= 0 || N <= 0 || taps <= 0)
-    return A8_ERR_ARG;
+// xin: fp16 [rows, ctx + T, Cin]; w: fp16 [N, taps * Cin] (K-major). Outputs as in ConvArgs (set by the caller).
+int conv_plan(ConvPlan* p, const void* xin, int rows, int T, int Cin, int ctx, const void* w, int N, int taps,
+              int dil) {
+  if (xin == nullptr || w == nullptr || rows <= 0 || T <= 0 || Cin <= 0 || N <= 0 || taps <= 0) return A8_ERR_ARG;
   if (Cin % 32) return A8_ERR_ARG;
   if ((taps - 1) * dil > ctx) return A8_ERR_ARG;
   ConvArgs& a = p->args;
+  a = ConvArgs{};
   a.rows = rows;
   a.T = T;
   a.Cin = Cin;
@@ -217,19 +469,12 @@ int conv_plan(ConvPlan* p, const void* xin, int rows, int T, int Cin, int ctx, c
   const int nt = (N + 255) / 256;
   a.ntile = std::max(16, ((N + nt - 1) / nt + 15) / 16 * 16);
   a.n_tiles = (N + a.ntile - 1) / a.ntile;
+  a.m_tiles = (T / a.TT) * ((rows + a.TB - 1) / a.TB);
   a.kb_total = taps * (Cin / a.KC);
-  a.tmem_cols = a.ntile <= 32 ? 32 : a.ntile <= 64 ? 64 : a.ntile <= 128 ? 128 : 256;
+  a.acc_cols = a.ntile <= 32 ? 32 : a.ntile <= 64 ? 64 : a.ntile <= 128 ? 128 : 256;
   const int stage_bytes = 128 * a.KC * 2 + a.ntile * a.KC * 2;
-  a.stages = std::max(2, std::min(6, (200 * 1024) / stage_bytes));
-  a.stages = std::min(a.stages, std::max(2, a.kb_total));
-  a.bias = reinterpret_cast<const __half*>(bias);
-  a.res = reinterpret_cast<const __half*>(res);
-  a.res_bs = res_bs;
-  a.res_ts = res_ts;
-  a.out = out;
-  a.out_bs = out_bs;
-  a.out_ts = out_ts;
-  a.mode = mode;
+  a.stages = std::max(2, std::min(8, (176 * 1024) / stage_bytes));   // room for the staged column constants
+  a.cout = N;
   const CUtensorMapSwizzle sw = a.KC == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   int rc = encode_map_3d(&p->tmX, xin, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Cin, ctx + T, rows, (uint64_t)Cin * 2,
                          (uint64_t)(ctx + T) * Cin * 2, a.KC, a.TT, a.TB, sw);
@@ -237,16 +482,45 @@ int conv_plan(ConvPlan* p, const void* xin, int rows, int T, int Cin, int ctx, c
   rc = encode_map_2d(&p->tmW, w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)taps * Cin, N, (uint64_t)taps * Cin * 2,
                      a.KC, a.ntile, sw);
   if (rc) return rc;
-  p->grid = dim3((T / a.TT) * ((rows + a.TB - 1) / a.TB), a.n_tiles);
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+  }
+  const int total = a.m_tiles * a.n_tiles;
+  p->grid = dim3(std::min(total, sms));
   p->smem = a.stages * stage_bytes + 1024 + 256;
   return A8_OK;
 }
 
+// The outputs' alignment: 16-element row segments are stored as 32-byte vectors.
+static int conv_check_outputs(const ConvArgs& a) {
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31) == 0; };
+  if (a.audio == nullptr && a.raw == nullptr && a.nxt == nullptr) return A8_ERR_ARG;
+  if (a.N % 16 == 0) {
+    if (a.raw != nullptr && (!al(a.raw) || a.raw_bs % 16 || a.raw_ts % 16)) return A8_ERR_ALIGN;
+    if (a.res != nullptr && (!al(a.res) || a.res_bs % 16 || a.res_ts % 16)) return A8_ERR_ALIGN;
+    if (a.nxt != nullptr && (!al(a.nxt) || a.nxt_bs % 16 || a.nxt_off % 16)) return A8_ERR_ALIGN;
+    if (a.bias != nullptr && !al(a.bias)) return A8_ERR_ALIGN;
+    if (a.alpha != nullptr && (a.cout % 16 || (reinterpret_cast<uintptr_t>(a.alpha) & 15) ||
+                               (reinterpret_cast<uintptr_t>(a.inv) & 15)))
+      return A8_ERR_ALIGN;
+  }
+  if (a.alpha != nullptr && (a.inv == nullptr || a.cout <= 0 || a.N % a.cout)) return A8_ERR_ARG;
+  return A8_OK;
+}
+
 int conv_launch(const ConvPlan* p, cudaStream_t s) {
+  int rc = conv_check_outputs(p->args);
+  if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = p->grid;
-  cfg.blockDim = dim3(128);
-  cfg.dynamicSmemBytes = p->smem;
+  cfg.blockDim = dim3(CONV_THREADS);
+  const ConvArgs& a = p->args;
+  const int params = ((a.bias != nullptr ? (a.N + 3) / 4 * 4 : 0) + 2 * ((a.cout + 3) / 4 * 4)) * 4;
+  cfg.dynamicSmemBytes = p->smem + params;
+  if (cfg.dynamicSmemBytes > 227 * 1024) return A8_ERR_SIZE;
   cfg.stream = s;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -273,16 +547,49 @@ int conv_launch(const ConvPlan* p, cudaStream_t s) {
   return e == cudaSuccess ? A8_OK : A8_ERR_CUDA;
 }
 
+int ctx_shift_launch(const A8CtxShift* tab_dev, int n, int rows, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(n, rows);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  ++g_launches;
+  return cudaLaunchKernelEx(&cfg, k_ctx_shift, tab_dev, rows) == cudaSuccess ? A8_OK : A8_ERR_CUDA;
+}
+
 }  // namespace a8
 
 using namespace a8;
 
-extern "C" int a8_conv(const void* xin, int rows, int T, int Cin, int ctx, const void* w, int N, int taps, int dil,
-                       const void* bias, const void* res, long long res_bs, long long res_ts, void* out,
-                       long long out_bs, long long out_ts, int mode, a8_stream_t stream) {
+extern "C" int a8_conv(const A8ConvRun* r, a8_stream_t stream) {
+  if (r == nullptr) return A8_ERR_ARG;
   ConvPlan p;
-  int rc = conv_plan(&p, xin, rows, T, Cin, ctx, w, N, taps, dil, bias, res, res_bs, res_ts, out, out_bs, out_ts,
-                     mode);
+  int rc = conv_plan(&p, r->xin, r->rows, r->T, r->Cin, r->ctx, r->w, r->N, r->taps, r->dil);
   if (rc) return rc;
+  ConvArgs& a = p.args;
+  a.bias = reinterpret_cast<const float*>(r->bias);
+  a.res = reinterpret_cast<const __half*>(r->res);
+  a.res_bs = r->res_bs;
+  a.res_ts = r->res_ts;
+  a.raw = reinterpret_cast<__half*>(r->raw);
+  a.raw_bs = r->raw_bs;
+  a.raw_ts = r->raw_ts;
+  a.nxt = reinterpret_cast<__half*>(r->nxt);
+  a.nxt_bs = r->nxt_bs;
+  a.nxt_off = r->nxt_off;
+  a.cout = r->cout > 0 ? r->cout : r->N;
+  a.alpha = r->alpha;
+  a.inv = r->inv;
+  a.audio = r->audio;
+  a.audio_bs = r->audio_bs;
   return conv_launch(&p, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int a8_ctx_shift(const A8CtxShift* table, int n, int rows, a8_stream_t stream) {
+  if (table == nullptr || n <= 0 || rows <= 0) return A8_ERR_ARG;
+  return ctx_shift_launch(table, n, rows, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -10,6 +10,7 @@
 namespace a8 {
 
 int stack_forward(const A8StackDesc& d, const A8StackRun& r, cudaStream_t s);
+int voc_decode(const A8Vocoder& v, const void* u, int b, cudaStream_t s);
 
 static int voc_gemm(const void* x, int ldx, const void* w, int N, int K, int M, void* y, int ldy, const A8Epilogue& e,
                     cudaStream_t s) {
@@ -66,26 +67,53 @@ int voc_step(const A8Vocoder& v, const int64_t* codes, int b, cudaStream_t s, cu
     xs = v.ubuf[3];
   }
 
-  // conv program
+  return voc_decode(v, xs, b, s);
+}
+
+// The conv decoder on u (bf16 [b, T0, C], T0 = the first op's T): the first op's input rows from u; each op's epilogue
+// writes the next op's input rows (activated) and, where a later residual needs it, its raw output; the last op writes
+// the audio; then every context advances one frame.
+int voc_decode(const A8Vocoder& v, const void* u, int b, cudaStream_t s) {
+  if (b <= 0 || b > v.B || v.n_ops > A8_MAX_CONV_OPS || v.n_ops <= 0) return A8_ERR_ARG;
+  const A8ConvOp& op0 = v.ops[0];
+  int rc = conv_input(u, 1, (long long)op0.T * op0.Cin, op0.T, op0.Cin, op0.xin, op0.ctx, op0.alpha, op0.inv, b, s);
+  if (rc) return rc;
   for (int i = 0; i < v.n_ops; ++i) {
     const A8ConvOp& op = v.ops[i];
-    if (op.in < -1 || op.in > 2 || op.out < -1 || op.out > 2 || op.res < -1 || op.res > 2) return A8_ERR_ARG;
-    const void* src = op.in < 0 ? xs : v.act[op.in];
-    rc = snake_cat(src, op.in < 0 ? 1 : 0, (long long)op.T * op.Cin, op.T, op.Cin, op.state, op.state_bs, op.ctx,
-                   op.alpha, op.inv, v.xin, b, s);
-    if (rc) return rc;
-    const void* res = op.res >= 0 ? v.act[op.res] : nullptr;
-    const long long rbs = res != nullptr ? (long long)op.T * op.N : 0, rts = res != nullptr ? op.N : 0;
+    if (op.raw < -1 || op.raw > 1 || op.res < -1 || op.res > 1 || op.xin == nullptr) return A8_ERR_ARG;
     ConvPlan p;
-    if (op.out < 0)
-      rc = conv_plan(&p, v.xin, b, op.T, op.Cin, op.ctx, op.w, op.N, op.taps, op.dil, op.bias, nullptr, 0, 0, v.audio,
-                     v.up, 1, 1);
-    else
-      rc = conv_plan(&p, v.xin, b, op.T, op.Cin, op.ctx, op.w, op.N, op.taps, op.dil, op.bias, res, rbs, rts,
-                     v.act[op.out], (long long)op.T * op.N, op.N, 0);
-    if (rc) return rc;
+    if ((rc = conv_plan(&p, op.xin, b, op.T, op.Cin, op.ctx, op.w, op.N, op.taps, op.dil))) return rc;
+    ConvArgs& a = p.args;
+    a.bias = reinterpret_cast<const float*>(op.bias);
+    if (op.res >= 0) {
+      a.res = reinterpret_cast<const __half*>(v.act[op.res]);
+      a.res_bs = (long long)op.T * op.N;
+      a.res_ts = op.N;
+    }
+    if (op.raw >= 0) {
+      a.raw = reinterpret_cast<__half*>(v.act[op.raw]);
+      a.raw_bs = (long long)op.T * op.N;
+      a.raw_ts = op.N;
+    }
+    if (i + 1 < v.n_ops) {
+      const A8ConvOp& nx = v.ops[i + 1];
+      if (op.N % nx.Cin || nx.T != op.T * (op.N / nx.Cin)) return A8_ERR_ARG;
+      a.nxt = reinterpret_cast<__half*>(nx.xin);
+      a.nxt_bs = (long long)(nx.ctx + nx.T) * nx.Cin;
+      a.nxt_off = (long long)nx.ctx * nx.Cin;
+      a.cout = nx.Cin;
+      a.alpha = nx.alpha;
+      a.inv = nx.inv;
+    } else {
+      if (op.T != v.up) return A8_ERR_ARG;
+      a.audio = v.audio;
+      a.audio_bs = v.up;
+    }
+    if (v.conv_ctas > 0 && (int)p.grid.x > v.conv_ctas) p.grid.x = v.conv_ctas;
     if ((rc = conv_launch(&p, s))) return rc;
   }
+  // every context advances one frame
+  if (v.n_ctx > 0 && (rc = ctx_shift_launch(v.ctx_table, v.n_ctx, b, s))) return rc;
   return A8_OK;
 }
 
@@ -132,6 +160,11 @@ using namespace a8;
 extern "C" int a8_voc_step(const A8Vocoder* v, const int64_t* codes, int b, a8_stream_t stream) {
   if (v == nullptr || codes == nullptr) return A8_ERR_ARG;
   return voc_step(*v, codes, b, reinterpret_cast<cudaStream_t>(stream), nullptr);
+}
+
+extern "C" int a8_voc_decode(const A8Vocoder* v, const void* u, int b, a8_stream_t stream) {
+  if (v == nullptr || u == nullptr) return A8_ERR_ARG;
+  return voc_decode(*v, u, b, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int a8_state_rows(const A8StateSeg* segs, int nseg, const int* slots, int nslots, int op, void* blob,

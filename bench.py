@@ -533,6 +533,8 @@ def conv_roofline(eng, L, dev, b, args):
     """Each decoder conv of the codec step timed alone (CUDA events around each launch on its stream, L2 flushed
     between launches); the roofline line is the conv with the largest total time (tensor-bound: its algorithmic
     FLOPs / duration against the measured bf16 peak; fp16 and bf16 run at the same tensor-core rate)."""
+    import ctypes as C
+
     import torch
     _, tf, kind = _peaks()
     voc = eng.voc
@@ -540,16 +542,13 @@ def conv_roofline(eng, L, dev, b, args):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     reps = max(3, min(10, args.steps))
     res = []
-    for i, (c, T, src, dst, rr) in enumerate(voc.ops):
-        out, obs, ots, mode = (voc.audio, voc.up, 1, 1) if dst < 0 else (voc.act[dst], T * c.N, c.N, 0)
-        r = voc.act[rr] if rr >= 0 else None
-        args_ = (L.ptr(voc.xin), b, T, c.Cin, c.ctx, L.ptr(c.w), c.N, c.taps, c.dil, L.ptr(c.bias), L.ptr(r),
-                 T * c.N if r is not None else 0, c.N if r is not None else 0, L.ptr(out), obs, ots, mode)
+    for i, (c, T, *_) in enumerate(voc.ops):
+        run = voc.conv_run(i, b)
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps + 2)]
         for k, (a, z) in enumerate(ev):
             flush.zero_()
             a.record()
-            L.call("a8_conv", *args_, L.stream_handle())
+            L.call("a8_conv", C.byref(run), L.stream_handle())
             z.record()
         torch.cuda.synchronize()
         t = sum(a.elapsed_time(z) for a, z in ev[2:]) / reps / 1000.0

@@ -128,27 +128,55 @@ int a8_tick_start(const int64_t* tok, int64_t* tok_in, int64_t* codes, int ncb, 
 int a8_gather_rows(const void* src, int lds, const int* idx, void* y, int ldy, int rows, int H, a8_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------------- codec */
-/* Channels-last causal conv / polyphase transposed conv as an implicit GEMM, fp16 in, fp32 accumulation
- * (serve/fast_kernels.py:551-623 conv_cl, serve/fast_engine.py:218-232 _CLConv.__call__):
+/* One launch of the decoder conv (serve/fast_kernels.py:551-623 conv_cl, serve/fast_engine.py:218-232 _CLConv):
  *   y[b, t, n] = bias[n] + sum_{j < taps} sum_c xin[b, t + j*dil, c] * w[n, j*Cin + c]  (+ res[b*res_bs + t*res_ts + n])
- * xin fp16 [rows, ctx + T, Cin] (Cin a multiple of 32, (taps-1)*dil <= ctx), w fp16 [N, taps*Cin] with N padded to a
- * multiple of 16 (a transposed conv of stride s: N = s*Cout, n = p*Cout + c, row t holds output rows t*s+p).
- * mode 0: fp16 y at out[b*out_bs + t*out_ts + n]; mode 1 (conv_out): fp32 tanh(fp16(y[b, t, 0])) at out[b*out_bs + t].
- * T a power of two (or any T with T % min(T,128) == 0 and 128 % min(T,128) == 0). */
-int a8_conv(const void* xin, int rows, int T, int Cin, int ctx, const void* w, int N, int taps, int dil,
-            const void* bias, const void* res, long long res_bs, long long res_ts, void* out, long long out_bs,
-            long long out_ts, int mode, a8_stream_t stream);
-/* A conv's context-padded input (serve/fast_kernels.py:695-729 snake_cat, serve/fast_engine.py:226-231):
- * xin[b] = [state[b] (ctx rows) ; fp16(snake(x[b]))], then state[b] = xin[b, T:T+ctx]. x is fp16 (x_bf16 = 0) or
- * bf16 rows of C at batch stride x_bs elements, state rows state_bs elements apart; snake(v) = v + inv * sin(alpha v)^2 in fp32 (alpha NULL: identity);
- * ctx = 0: no state. C a multiple of 8. */
-int a8_snake_cat(const void* x, int x_bf16, long long x_bs, int T, int C, void* state, long long state_bs, int ctx,
-                 const float* alpha, const float* inv, void* xin, int rows, a8_stream_t stream);
+ * for t in [0, T), accumulated in fp32 on the tensor cores and rounded to fp16 once. xin fp16 [rows, ctx + T, Cin]
+ * holds the conv's carried context in rows [0, ctx) (Cin a multiple of 32, (taps-1)*dil <= ctx; T with
+ * T % min(T,128) == 0 and 128 % min(T,128) == 0). w fp16 [N, taps*Cin]; a transposed conv of stride s is 2 taps with
+ * N = s*Cout, n = p*Cout + c, so row t holds output timesteps t*s + p. Outputs, any of:
+ *   raw   fp16 y at raw[b*raw_bs + t*raw_ts + n]
+ *   nxt   the NEXT conv's input rows, act(y) at nxt[b*nxt_bs + nxt_off + t*N + n], act(v) = v + inv[c] sin(alpha[c] v)^2
+ *         on the fp16 y (c = n % cout; alpha NULL: identity) -- the snake of serve/fast_kernels.py:578-583, :709-713
+ *   audio conv_out: audio[b*audio_bs + t] = tanh(fp16(y[b, t, 0])) (fp32)
+ * With N a multiple of 16, raw / res / nxt / bias are 32-byte aligned with strides multiples of 16 elements. */
+typedef struct A8ConvRun {
+  const void* xin;
+  int rows, T, Cin, ctx;
+  const void* w;
+  int N, taps, dil;
+  const float* bias;      /* [N] (the fp16 bias as fp32) or NULL */
+  const void* res;        /* fp16 or NULL */
+  long long res_bs, res_ts;
+  void* raw;              /* fp16 or NULL */
+  long long raw_bs, raw_ts;
+  void* nxt;              /* fp16 or NULL */
+  long long nxt_bs, nxt_off;
+  int cout;               /* channels of an output timestep (0: N) */
+  const float* alpha;     /* [cout] or NULL */
+  const float* inv;       /* [cout]: 1 / (alpha + 1e-9) */
+  float* audio;           /* or NULL */
+  long long audio_bs;
+} A8ConvRun;
+int a8_conv(const A8ConvRun* r, a8_stream_t stream);
+
+/* A conv's carried context for the next frame (serve/fast_engine.py:230-231): xin[b, :ctx] = xin[b, T : T + ctx] for
+ * rows [0, rows) of each table entry (the table in device memory; one launch for all of a step's convs). */
+typedef struct A8CtxShift {
+  void* xin;              /* fp16 [rows, ctx + T, Cin] */
+  int ctx, T, Cin;
+} A8CtxShift;
+int a8_ctx_shift(const A8CtxShift* table, int n, int rows, a8_stream_t stream);
+
+/* A conv's input rows from a tensor (serve/fast_kernels.py:695-729 snake_cat without the context, which lives in
+ * xin): xin[b, ctx + t, c] = fp16(act(x[b, t, c])) for x fp16 (x_bf16 = 0) or bf16 rows of C at batch stride x_bs
+ * elements, act as in a8_conv (alpha NULL: identity). C a multiple of 8. */
+int a8_conv_input(const void* x, int x_bf16, long long x_bs, int T, int C, void* xin, int ctx, const float* alpha,
+                  const float* inv, int rows, a8_stream_t stream);
 /* Upsample stage middle (serve/fast_engine.py:484-489): bf16 causal depthwise conv (K taps <= 8, carried tail
- * st [rows, K-1, C] at st_bs elements a row, every product and sum rounded to bf16 in tap order, bias first) and LayerNorm(eps) over C
- * (C a multiple of 128, <= 4096): z = bf16(LN(dwconv([st ; u]))), st = last K-1 input rows. */
-int a8_ups_dwln(const void* u, int T, int C, void* st, long long st_bs, int K, const void* dww, const void* dwb, const void* lnw,
-                const void* lnb, float eps, void* z, int rows, a8_stream_t stream);
+ * st [rows, K-1, C] at st_bs elements a row, every product and sum rounded to bf16 in tap order, bias first) and
+ * LayerNorm(eps) over C (C a multiple of 128, <= 4096): z = bf16(LN(dwconv([st ; u]))), st = last K-1 input rows. */
+int a8_ups_dwln(const void* u, int T, int C, void* st, long long st_bs, int K, const void* dww, const void* dwb,
+                const void* lnw, const void* lnb, float eps, void* z, int rows, a8_stream_t stream);
 /* Codec input (serve/fast_engine.py:472-477): x[r] = bf16(t_sem[clamp(codes[r,0])] + sum_k t_res[k, clamp(codes[r,k+1])])
  * (fp32 tables [v_sem, C] and [ncb-1, v_res, C]); pos_c[r] = min(pos[r], max_pos-1), lens[r] = min(pos[r]+1, window),
  * pos[r] += 1. */
@@ -214,18 +242,19 @@ typedef struct A8StackRun {
 int a8_stack_forward(const A8StackDesc* d, const A8StackRun* r, a8_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------------- streaming codec */
-/* One conv of the decoder program: xin = [context ; snake(in)] (a8_snake_cat), out = conv(xin) (+ res) (a8_conv). */
+/* One conv of the decoder program. Its input rows xin (context first, persistent across frames) are written by the
+ * previous op's epilogue with this op's activation; the first op's by a8_conv_input from the upsample output; the last
+ * op writes audio. */
 typedef struct A8ConvOp {
   const void* w;          /* fp16 [N, taps * Cin] */
-  const void* bias;       /* fp16 [N] or NULL */
-  const float* alpha;     /* snake alpha [Cin] or NULL (no activation) */
+  const float* bias;      /* [N] (the fp16 bias as fp32) or NULL */
+  const float* alpha;     /* the snake in front of this conv: alpha [Cin] or NULL (no activation) */
   const float* inv;       /* 1 / (alpha + 1e-9) [Cin] */
-  void* state;            /* fp16 context [slot rows, ctx, Cin] at state_bs elements a row, or NULL (ctx 0) */
-  long long state_bs;
+  void* xin;              /* fp16 [slot rows, ctx + T, Cin] */
   int Cin, N, taps, dil, ctx;
   int T;                  /* input timesteps a frame */
-  int in, out, res;       /* activation buffers act[i]; in -1: the upsample output (bf16); out -1: audio (tanh of
-                             column 0, fp32); res -1: none */
+  int raw;                /* act buffer receiving the raw output (a later residual), or -1 */
+  int res;                /* act buffer added to the output, or -1 */
 } A8ConvOp;
 
 /* One upsample stage ([transposed conv k = s = 2 as a GEMM, causal ConvNeXt block], serve/fast_engine.py:479-491). */
@@ -267,14 +296,20 @@ typedef struct A8Vocoder {
   void* ubuf[4];          /* bf16 scratch: [B * 2^n_ups, C] x3 and [B * 2^n_ups, mlp] */
   int n_ops;
   A8ConvOp ops[A8_MAX_CONV_OPS];
-  void* act[3];           /* fp16 scratch: each the largest [B, T, N] of the program */
-  void* xin;              /* fp16 scratch: the largest [B, ctx + T, Cin] */
+  void* act[2];           /* fp16 scratch for raw outputs: each the largest [B, T, N] of the program */
+  const A8CtxShift* ctx_table; /* device table of the ops with a context (a8_ctx_shift after the step) */
+  int n_ctx;
+  int conv_ctas;          /* persistent CTAs of each decoder conv (0: one per SM); fewer leave SMs to the tick's
+                             other stream */
   float* audio;           /* fp32 [B, up] */
 } A8Vocoder;
 
 /* StreamingVocoder.step (serve/fast_engine.py:470-494): one codec frame for rows [0, b): codes [b, ncb] (int64, row
  * stride ncb) -> audio [b, up]; every row's carried state advances one frame. */
 int a8_voc_step(const A8Vocoder* v, const int64_t* codes, int b, a8_stream_t stream);
+/* The conv decoder part of the step alone (serve/fast_engine.py:301-309 _CLDecoder.__call__): u bf16 [b, T0, C]
+ * (T0 = ops[0].T) -> audio [b, up]; every conv context advances one frame. */
+int a8_voc_decode(const A8Vocoder* v, const void* u, int b, a8_stream_t stream);
 
 /* A piece of per-slot state: for every slot, nchunks chunks of chunk_bytes at base + slot * slot_stride +
  * k * chunk_stride (addresses and sizes multiples of 4 bytes; 16 for the vector path); in a snapshot it sits at

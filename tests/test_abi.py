@@ -39,7 +39,8 @@ def test_struct_layouts_match_header(a8):
     src = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
     for cname, cls in (("A8Epilogue", L.A8Epilogue), ("A8Scratch", L.A8Scratch), ("A8StackDesc", L.A8StackDesc),
                        ("A8StackRun", L.A8StackRun), ("A8Engine", L.A8Engine), ("A8ConvOp", L.A8ConvOp),
-                       ("A8Upsample", L.A8Upsample), ("A8Vocoder", L.A8Vocoder), ("A8StateSeg", L.A8StateSeg)):
+                       ("A8Upsample", L.A8Upsample), ("A8Vocoder", L.A8Vocoder), ("A8StateSeg", L.A8StateSeg),
+                       ("A8ConvRun", L.A8ConvRun), ("A8CtxShift", L.A8CtxShift)):
         body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), src, flags=re.S).group(1)
         fields = []
         for decl in body.split(";"):
@@ -70,7 +71,8 @@ def test_struct_sizes_match_c_compiler(a8, tmp_path):
     L = a8._lib
     structs = {"A8Epilogue": L.A8Epilogue, "A8Scratch": L.A8Scratch, "A8StackDesc": L.A8StackDesc,
                "A8StackRun": L.A8StackRun, "A8Engine": L.A8Engine, "A8ConvOp": L.A8ConvOp,
-               "A8Upsample": L.A8Upsample, "A8Vocoder": L.A8Vocoder, "A8StateSeg": L.A8StateSeg}
+               "A8Upsample": L.A8Upsample, "A8Vocoder": L.A8Vocoder, "A8StateSeg": L.A8StateSeg,
+               "A8ConvRun": L.A8ConvRun, "A8CtxShift": L.A8CtxShift}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "audio8_b200.h"', 'int main(void) {']
     for cname, cls in structs.items():
         lines.append(f'printf("{cname} sizeof %zu\\n", sizeof({cname}));')

@@ -85,20 +85,11 @@ def test_vocoder_frames_match_oracle(a8, dev, tiny_model):
         assert s >= 40.0, (r, s)
 
 
-def gpu_decode(L, voc, u, b):
-    """The decoder's conv program alone (the ops a8_voc_step runs after the upsample) on u [b, T, C]."""
-    ub = u.to(BF).to(voc.dev).contiguous()
-    for c, T, src, dst, res in voc.ops:
-        x = ub if src < 0 else voc.act[src]
-        L.call("a8_snake_cat", L.ptr(x), int(src < 0), T * c.Cin, T, c.Cin, L.ptr(c.state), c.ctx * c.Cin, c.ctx,
-               L.ptr(c.alpha), L.ptr(c.inv), L.ptr(voc.xin), b, L.stream_handle())
-        out, obs, ots, mode = (voc.audio, voc.up, 1, 1) if dst < 0 else (voc.act[dst], T * c.N, c.N, 0)
-        r = voc.act[res] if res >= 0 else None
-        L.call("a8_conv", L.ptr(voc.xin), b, T, c.Cin, c.ctx, L.ptr(c.w), c.N, c.taps, c.dil, L.ptr(c.bias), L.ptr(r),
-               T * c.N if r is not None else 0, c.N if r is not None else 0, L.ptr(out), obs, ots, mode,
-               L.stream_handle())
+def gpu_decode(voc, u, b):
+    """The decoder's conv program alone (a8_voc_decode) on u [b, T, C]."""
+    wav = voc.decode(u.to(voc.dev), b)
     torch.cuda.synchronize()
-    return voc.audio[:b].cpu().clone()
+    return wav.cpu().clone()
 
 
 def test_vocoder_decoder_matches_oracle(a8, dev, tiny_model):
@@ -111,7 +102,7 @@ def test_vocoder_decoder_matches_oracle(a8, dev, tiny_model):
     g = torch.Generator().manual_seed(13)
     for f in range(3):
         u = R.bf(torch.randn(b, 4, cfg.codec_dim, generator=g))
-        wav = gpu_decode(a8._lib, voc, u, b)
+        wav = gpu_decode(voc, u, b)
         wav_o = ora.decode(u, b)
         assert a8.device_error()[0] == 0
         for r in range(b):
