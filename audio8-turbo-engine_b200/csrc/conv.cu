@@ -61,38 +61,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// fp32 <-> fp16 on the IEEE-754 fields with integer arithmetic, so the epilogue's many conversions run on the integer
-// pipes instead of the conversion unit. to_f16: round to nearest even, returning the fp16 bits and (in r) the
-// rounded value as fp32; exact for results in the fp16 normal range below 2^15 (|v| in [2^-14, 32768)), the
-// conversion instruction for everything else (zero, subnormal, large, inf, nan).
-__device__ __forceinline__ uint32_t to_f16(float v, float& r) {
-  const uint32_t u = __float_as_uint(v);
-  const uint32_t e = (u >> 23) & 0xFFu;
-  if (e - 113u <= 28u) {                             // biased fp32 exponent 113..141
-    const uint32_t q = (u + 0xFFFu + ((u >> 13) & 1u)) & 0xFFFFE000u;
-    r = __uint_as_float(q);
-    return ((q >> 16) & 0x8000u) | ((((q >> 23) & 0xFFu) - 112u) << 10) | ((q >> 13) & 0x3FFu);
-  }
-  const __half h = __float2half_rn(v);
-  r = __half2float(h);
-  return __half_as_ushort(h);
-}
-// Branch-free forms of the two conversions for the epilogue's hot path: valid for fp16 normal numbers (and, for
-// f32_to_f16_fast, results below 2^15); `ok` is cleared for any other input, and the caller redoes such a chunk with
-// the exact conversions. f32_to_f16_fast rounds v to nearest even in place and returns the fp16 bits.
-__device__ __forceinline__ uint32_t f32_to_f16_fast(float& v, bool& ok) {
-  const uint32_t u = __float_as_uint(v);
-  ok &= ((u >> 23) & 0xFFu) - 113u <= 28u;
-  const uint32_t q = (u + 0xFFFu + ((u >> 13) & 1u)) & 0xFFFFE000u;
-  v = __uint_as_float(q);
-  return ((q >> 16) & 0x8000u) | ((((q >> 23) & 0xFFu) - 112u) << 10) | ((q >> 13) & 0x3FFu);
-}
-__device__ __forceinline__ float f16_to_f32_fast(uint32_t h, bool& ok) {
-  const uint32_t e = (h >> 10) & 0x1Fu;
-  ok &= e - 1u < 30u;
-  return __uint_as_float(((h & 0x8000u) << 16) | ((e + 112u) << 23) | ((h & 0x3FFu) << 13));
-}
-
 // sin^2(t) for |t| < 2^15 without branches: t = k pi/2 + r with k = rint(2t/pi) (round-to-nearest by adding 1.5 2^23)
 // and r = t - k pi/2 by a two-term split of pi/2 (Cody-Waite reduction with fused multiply-adds); then
 // sin^2(r) = r^2 P(r^2) with P the Taylor series of (sin r / r)^2 = sum_n (-1)^n 2^(2n+1) r^(2n) / (2n+2)!, which for
@@ -113,14 +81,6 @@ __device__ __forceinline__ float sin2_reduced(float t) {
   p = fmaf(p, u, 1.0f);                                  // 2 / 2!
   const float s2 = u * p;
   return odd ? 1.0f - s2 : s2;
-}
-
-// fp16 bits -> fp32 (exact): normal numbers and zeros by field arithmetic, the rest by the conversion instruction
-__device__ __forceinline__ float from_f16(uint32_t h) {
-  const uint32_t e = (h >> 10) & 0x1Fu;
-  if (e - 1u < 30u) return __uint_as_float(((h & 0x8000u) << 16) | ((e + 112u) << 23) | ((h & 0x3FFu) << 13));
-  if ((h & 0x7FFFu) == 0) return __uint_as_float((h & 0x8000u) << 16);
-  return __half2float(__ushort_as_half(static_cast<unsigned short>(h)));
 }
 
 // The epilogue of one 16-column chunk with the exact conversions and sinf, from the raw accumulators v: fp16 y into
@@ -310,21 +270,26 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
           tmem_ld16(trow, v);
           if (live) {
             const float bias = a.bias != nullptr ? a.bias[0] : 0.f;
-            float y;
-            to_f16(v[0] + bias, y);
-            a.audio[(size_t)b * a.audio_bs + t] = tanhf(y);
+            a.audio[(size_t)b * a.audio_bs + t] = tanhf(f16r(v[0] + bias));
           }
         }
       } else {
         for (int ch = part; ch < nchunk; ch += PARTS) {
           const int nb = n0 + ch * 16;
           if (nb >= a.N) break;                // warp-uniform
+          const int nn = min(16, a.N - nb);
+          const bool has_res = a.res != nullptr && live && nn == 16;
+          uint4 r0 = make_uint4(0, 0, 0, 0), r1 = r0;
+          if (has_res) {                       // the residual's latency overlaps the TMEM read
+            const uint4* rp = reinterpret_cast<const uint4*>(a.res + (size_t)b * a.res_bs + (size_t)t * a.res_ts + nb);
+            r0 = rp[0];
+            r1 = rp[1];
+          }
           float v[16];
           tmem_ld16(trow + ch * 16, v);
-          const int nn = min(16, a.N - nb);
           if (nn == 16) {
-            // straight-line fast path (no branches, so the 16 columns interleave); a chunk where any value leaves
-            // the fast path's range is redone exactly below (warp-uniform)
+            // straight-line fast path (so the 16 columns interleave); a chunk whose activation argument leaves the
+            // range of sin2_reduced is redone with sinf below (warp-uniform)
             bool ok = true;
             const bool act = a.nxt != nullptr && a.alpha != nullptr;
             uint32_t hy[8], ha[8];
@@ -338,20 +303,21 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
                 v[i + 3] += bv.w;
               }
             }
-            if (a.res != nullptr && live) {
-              const uint4* rp = reinterpret_cast<const uint4*>(a.res + (size_t)b * a.res_bs + (size_t)t * a.res_ts + nb);
-              const uint4 r0 = rp[0], r1 = rp[1];
+            if (has_res) {
               const uint32_t w[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
 #pragma unroll
               for (int i = 0; i < 8; ++i) {
-                v[2 * i] += f16_to_f32_fast(w[i] & 0xFFFFu, ok);
-                v[2 * i + 1] += f16_to_f32_fast(w[i] >> 16, ok);
+                const float2 f = unpack_f16(w[i]);
+                v[2 * i] += f.x;
+                v[2 * i + 1] += f.y;
               }
             }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {                    // v becomes the fp16 y (as fp32)
-              const uint32_t lo = f32_to_f16_fast(v[2 * i], ok), hi = f32_to_f16_fast(v[2 * i + 1], ok);
-              hy[i] = lo | (hi << 16);
+            for (int i = 0; i < 8; ++i) {                    // fp16 y, and v becomes it (as fp32)
+              hy[i] = pack_f16(v[2 * i], v[2 * i + 1]);
+              const float2 f = unpack_f16(hy[i]);
+              v[2 * i] = f.x;
+              v[2 * i + 1] = f.y;
             }
             if (act) {
               const int c = nb % a.cout;
@@ -360,19 +326,18 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
                 const float4 al = *reinterpret_cast<const float4*>(s_alpha + c + i);
                 const float4 iv = *reinterpret_cast<const float4*>(s_inv + c + i);
                 const float al4[4] = {al.x, al.y, al.z, al.w}, iv4[4] = {iv.x, iv.y, iv.z, iv.w};
-                uint32_t h[4];
+                float z[4];
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                   const float tt = v[i + k] * al4[k];
                   ok &= fabsf(tt) < 32768.f;
-                  float y = fmaf(iv4[k], sin2_reduced(tt), v[i + k]);
-                  h[k] = f32_to_f16_fast(y, ok);
+                  z[k] = fmaf(iv4[k], sin2_reduced(tt), v[i + k]);
                 }
-                ha[i / 2] = h[0] | (h[1] << 16);
-                ha[i / 2 + 1] = h[2] | (h[3] << 16);
+                ha[i / 2] = pack_f16(z[0], z[1]);
+                ha[i / 2 + 1] = pack_f16(z[2], z[3]);
               }
             }
-            if (!__all_sync(0xffffffffu, ok || !live)) {   // rare: zeros, subnormals, huge values
+            if (!__all_sync(0xffffffffu, ok || !live)) {   // rare: |alpha y| >= 2^15
               tmem_ld16(trow + ch * 16, v);
               if (live) exact_chunk(a, v, b, t, nb, act, hy, ha);
             }
