@@ -32,6 +32,12 @@ struct ConvArgs {
   int TT, TB;               // token tile: TB batch rows x TT timesteps (TT * TB == 128)
   int ntile, n_tiles, m_tiles;
   int kb_total, stages;
+  // slab mode (TT = 128, one batch row a unit): the unit's input rows [t0, t0 + R) of one channel block are
+  // loaded ONCE (a slab) and every tap reads it at row offset j*dil; weights stream through their own ring
+  int slab, R, na, nb;
+  int sub;                  // 128-row sub-tiles a unit (slab mode: 2 share every weight tile; else 1)
+  int hb;                   // slab rows a TMA box (a slab of R rows is ceil(R / hb) boxes)
+  uint32_t a_slot;          // bytes of one slab slot
   uint32_t acc_cols;        // TMEM columns of one accumulator (power of two >= ntile)
   const float* bias;        // [N] (fp16 values as fp32) or null
   const __half* res;        // [b*res_bs + t*res_ts + n] or null
@@ -59,6 +65,18 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// UMMA descriptor of a 128B-swizzled K-major tile starting at any 128-byte row of a tile that TMA wrote from a
+// 1024-aligned base: the swizzle is a function of the absolute shared-memory address, so a row offset is a plain
+// start-address offset (matrix base offset 0). Checked on the GPU for row offsets 0..54 (dilations 1, 3, 8, 9): a
+// base offset of (addr >> 7) & 7 gives wrong products, 0 gives the exact ones.
+__device__ __forceinline__ uint64_t umma_desc_sw128_row(uint32_t addr) {
+  return ((uint64_t)((addr >> 4) & 0x3FFFu)) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+// the same for a 64B-swizzled tile (64-byte rows, 8-row groups 512 B apart)
+__device__ __forceinline__ uint64_t umma_desc_sw64_row(uint32_t addr) {
+  return ((uint64_t)((addr >> 4) & 0x3FFFu)) | (1ull << 16) | (32ull << 32) | (1ull << 46) | (4ull << 61);
 }
 
 // sin^2(t) for |t| < 2^15 without branches: t = k pi/2 + r with k = rint(2t/pi) (round-to-nearest by adding 1.5 2^23)
@@ -114,18 +132,21 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   const int stages = a.stages;
   const uint32_t a_bytes = 128 * KC * 2, b_bytes = a.ntile * KC * 2;
   const uint32_t stage_bytes = a_bytes + b_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * stage_bytes);
-  uint64_t* empty = full + stages;
-  uint64_t* tfull = empty + stages;       // [2] accumulator ready
+  // pipeline: `stages` slots of (A, B) -- or, in slab mode, na slab slots then nb weight slots
+  const uint32_t pipe_bytes = a.slab ? a.na * a.a_slot + a.nb * b_bytes : stages * stage_bytes;
+  const int nbar = a.slab ? a.na + a.nb : stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + pipe_bytes);
+  uint64_t* empty = full + nbar;
+  uint64_t* tfull = empty + nbar;         // [2] accumulator ready
   uint64_t* tempty = tfull + 2;           // [2] accumulator drained
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   // the epilogue's per-column constants, staged once: bias [N], then alpha and inv [cout] (no global loads per tile)
-  float* s_bias = reinterpret_cast<float*>(smem + stages * stage_bytes + 256);
+  float* s_bias = reinterpret_cast<float*>(smem + pipe_bytes + 256);
   float* s_alpha = s_bias + (a.bias != nullptr ? (a.N + 3) / 4 * 4 : 0);
   float* s_inv = s_alpha + (a.cout + 3) / 4 * 4;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int tiles_t = a.T / a.TT;
+  const int tiles_t = a.T / (a.TT * a.sub);
   const int cblocks = a.Cin / KC;
   const int nkb = a.kb_total;
   const int total = a.m_tiles * a.n_tiles;
@@ -133,7 +154,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   if (tid == 0) {
     tma_prefetch(&tmX);
     tma_prefetch(&tmW);
-    for (int s = 0; s < stages; ++s) {
+    for (int s = 0; s < nbar; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -143,7 +164,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
     }
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 2 * a.acc_cols);
+  if (warp == 1) tmem_alloc(tmem_slot, 2 * a.sub * a.acc_cols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -155,11 +176,96 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   auto coords = [&](int tile, int* b0, int* t0, int* n0) {
     const int mt = tile / a.n_tiles, nt = tile % a.n_tiles;
     *b0 = (mt / tiles_t) * a.TB;
-    *t0 = (mt % tiles_t) * a.TT;
+    *t0 = (mt % tiles_t) * a.TT * a.sub;
     *n0 = nt * a.ntile;
   };
 
-  if (warp == 0) {
+  if (a.slab) {
+    // ------------------------------------------------------------------ slab mode
+    // order of use: for each unit, for each channel block c: the slab (A slot), then the taps' weight tiles (B slots)
+    auto slotA = [&](int s) { return smem + s * a.a_slot; };
+    auto slotB = [&](int s) { return smem + a.na * a.a_slot + s * b_bytes; };
+    uint64_t *fullA = full, *emptyA = empty, *fullB = full + a.na, *emptyB = empty + a.na;
+    if (warp == 0 && lane == 0) {
+      const uint64_t pol_w = policy_evict_last(), pol_x = policy_evict_first();
+      const int nbox = (a.R + a.hb - 1) / a.hb;
+      const uint32_t box_bytes = a.hb * KC * 2, slab_bytes = nbox * box_bytes;
+      int qa = 0, qb = 0;
+      bool ok = true;
+      // the first unit's first weight tiles do not depend on the previous kernel: issue them before waiting for it
+      const int pre = blockIdx.x < total ? min(a.nb, a.taps) : 0;
+      if (pre > 0) {
+        int b0, t0, n0;
+        coords(blockIdx.x, &b0, &t0, &n0);
+        for (int j = 0; j < pre; ++j) {
+          mbar_arrive_expect_tx(&fullB[j], b_bytes);
+          tma_load_2d(slotB(j), &tmW, &fullB[j], j * a.Cin, n0, pol_w);
+        }
+      }
+      pdl_wait();
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        int b0, t0, n0;
+        coords(tile, &b0, &t0, &n0);
+        for (int c = 0; c < cblocks && ok; ++c) {
+          const int sa = qa % a.na;
+          if (!(ok = mbar_wait(&emptyA[sa], ((qa / a.na) & 1) ^ 1, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
+          mbar_arrive_expect_tx(&fullA[sa], slab_bytes);
+          for (int x = 0; x < nbox; ++x)       // rows past the end of the input read as zeros (and go unused)
+            tma_load_3d(slotA(sa) + x * box_bytes, &tmX, &fullA[sa], c * KC, t0 + x * a.hb, b0, pol_x);
+          ++qa;
+          for (int j = 0; j < a.taps; ++j) {
+            if (qb < pre) {                        // issued before the wait
+              ++qb;
+              continue;
+            }
+            const int sb = qb % a.nb;
+            if (!(ok = mbar_wait(&emptyB[sb], ((qb / a.nb) & 1) ^ 1, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
+            mbar_arrive_expect_tx(&fullB[sb], b_bytes);
+            tma_load_2d(slotB(sb), &tmW, &fullB[sb], j * a.Cin + c * KC, n0, pol_w);
+            ++qb;
+          }
+        }
+      }
+      // every load issued has landed before the CTA can exit (also after a timeout)
+      for (int i = max(0, qa - a.na); i < qa; ++i)
+        mbar_wait(&fullA[i % a.na], (i / a.na) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
+      for (int i = max(0, qb - a.nb); i < qb; ++i)
+        mbar_wait(&fullB[i % a.nb], (i / a.nb) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
+    } else if (warp == 1 && lane == 0) {
+      const uint32_t idesc = umma_idesc(128, a.ntile, 0);   // fp16 x fp16 -> fp32
+      int qa = 0, qb = 0, it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
+        const int acc = it & 1, use = it >> 1;
+        if (!(ok = mbar_wait(&tempty[acc], (use & 1) ^ 1, ERR_TIMEOUT_ACCUM, KERNEL_ID_CONV))) break;
+        tc_fence_after();
+        const uint32_t d0 = tmem + acc * a.sub * a.acc_cols;
+        for (int c = 0; c < cblocks && ok; ++c) {
+          const int sa = qa % a.na;
+          if (!(ok = mbar_wait(&fullA[sa], (qa / a.na) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
+          const uint32_t slab = smem_u32(slotA(sa));
+          for (int j = 0; j < a.taps; ++j) {
+            const int sb = qb % a.nb;
+            if (!(ok = mbar_wait(&fullB[sb], (qb / a.nb) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
+            tc_fence_after();
+            const uint64_t db = KC == 64 ? umma_desc_sw128(slotB(sb)) : umma_desc_sw64(slotB(sb));
+            for (int s = 0; s < a.sub; ++s) {    // the sub-tiles share the weight tile
+              const uint32_t arow = slab + uint32_t(s * 128 + j * a.dil) * (KC * 2);
+              const uint64_t da = KC == 64 ? umma_desc_sw128_row(arow) : umma_desc_sw64_row(arow);
+              const uint32_t d = d0 + s * a.acc_cols;
+#pragma unroll
+              for (int k = 0; k < KC / 16; ++k) umma_f16(d, da + 2 * k, db + 2 * k, idesc, (c | j | k) != 0);
+            }
+            umma_commit(&emptyB[sb]);
+            ++qb;
+          }
+          umma_commit(&emptyA[sa]);
+          ++qa;
+        }
+        umma_commit(&tfull[acc]);             // (after a timeout too: the epilogue is not left waiting)
+      }
+    }
+  } else if (warp == 0) {
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_last(), pol_x = policy_evict_first();
       // the first tile's weights do not depend on the previous kernel: start them before waiting for it
@@ -233,7 +339,8 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
         umma_commit(&tfull[acc]);             // (after a timeout too: the epilogue is not left waiting)
       }
     }
-  } else {
+  }
+  if (warp >= 2) {
     // ---------------------------------------------------------------- epilogue warps
     const int ew = warp - 2;                  // 0 .. CONV_EPI_WARPS-1
     const int quarter = warp & 3;             // TMEM lanes [32 quarter, +32) are this warp's
@@ -261,22 +368,26 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       tc_fence_after();
       int b0, t0, n0;
       coords(tile, &b0, &t0, &n0);
-      const int b = b0 + r / a.TT, t = t0 + r % a.TT;
+      const int b = b0 + r / a.TT;
       const bool live = b < a.rows;
-      const uint32_t trow = tmem + acc * a.acc_cols + (uint32_t(quarter * 32) << 16);
+      const uint32_t tbase = tmem + acc * a.sub * a.acc_cols + (uint32_t(quarter * 32) << 16);
       if (a.audio != nullptr) {
-        if (part == 0) {
+        for (int s = part; s < a.sub; s += PARTS) {
           float v[16];
-          tmem_ld16(trow, v);
+          tmem_ld16(tbase + s * a.acc_cols, v);
           if (live) {
             const float bias = a.bias != nullptr ? a.bias[0] : 0.f;
-            a.audio[(size_t)b * a.audio_bs + t] = tanhf(f16r(v[0] + bias));
+            a.audio[(size_t)b * a.audio_bs + t0 + s * 128 + r % a.TT] = tanhf(f16r(v[0] + bias));
           }
         }
       } else {
-        for (int ch = part; ch < nchunk; ch += PARTS) {
+        // the unit's (sub-tile, 16-column chunk) pairs, round robin over the warps of this lane quarter
+        for (int f = part; f < a.sub * nchunk; f += PARTS) {
+          const int s = f / nchunk, ch = f % nchunk;
+          const int t = t0 + s * 128 + r % a.TT;
+          const uint32_t trow = tbase + s * a.acc_cols;
           const int nb = n0 + ch * 16;
-          if (nb >= a.N) break;                // warp-uniform
+          if (nb >= a.N) continue;             // warp-uniform
           const int nn = min(16, a.N - nb);
           const bool has_res = a.res != nullptr && live && nn == 16;
           uint4 r0 = make_uint4(0, 0, 0, 0), r1 = r0;
@@ -381,7 +492,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, 2 * a.acc_cols);
+  if (warp == 1) tmem_dealloc(tmem, 2 * a.sub * a.acc_cols);
 }
 
 // ------------------------------------------------------------------------------------------------ context shift
@@ -440,9 +551,30 @@ int conv_plan(ConvPlan* p, const void* xin, int rows, int T, int Cin, int ctx, c
   const int stage_bytes = 128 * a.KC * 2 + a.ntile * a.KC * 2;
   a.stages = std::max(2, std::min(8, (176 * 1024) / stage_bytes));   // room for the staged column constants
   a.cout = N;
+  // slab mode: units of one batch row, 128 steps -- or two 128-step sub-tiles sharing each weight tile when T allows
+  // and the output tile is at most 128 columns (the accumulator pairs stay double-buffered in 512 TMEM columns;
+  // narrowing a wider tile to get there measured slower: twice the MMA instructions at half the width)
+  a.sub = 1;
+  a.slab = (a.TT == 128 && taps > 1 && ctx <= 128) ? 1 : 0;
+  if (a.slab && T % 256 == 0 && a.ntile <= 128) a.sub = 2;
+  a.m_tiles = (T / (a.TT * a.sub)) * ((rows + a.TB - 1) / a.TB);
+  const int b_bytes = a.ntile * a.KC * 2;
+  if (a.slab) {
+    a.R = 128 * a.sub + ctx;
+    a.hb = a.R <= 256 ? a.R : ((a.R + 1) / 2 + 7) / 8 * 8;   // boxes of <= 256 rows, 8-row aligned
+    const int nbox = (a.R + a.hb - 1) / a.hb;
+    a.a_slot = ((uint32_t)nbox * a.hb * a.KC * 2 + 1023) / 1024 * 1024;
+    a.na = 2;
+    a.nb = std::min(8, (int)((176 * 1024 - a.na * a.a_slot) / b_bytes));
+    if (a.nb < 2) {
+      a.slab = 0;
+      a.sub = 1;
+      return A8_ERR_SIZE;                                    // (not reached with the decoder's shapes)
+    }
+  }
   const CUtensorMapSwizzle sw = a.KC == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   int rc = encode_map_3d(&p->tmX, xin, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Cin, ctx + T, rows, (uint64_t)Cin * 2,
-                         (uint64_t)(ctx + T) * Cin * 2, a.KC, a.TT, a.TB, sw);
+                         (uint64_t)(ctx + T) * Cin * 2, a.KC, a.slab ? a.hb : a.TT, a.slab ? 1 : a.TB, sw);
   if (rc) return rc;
   rc = encode_map_2d(&p->tmW, w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)taps * Cin, N, (uint64_t)taps * Cin * 2,
                      a.KC, a.ntile, sw);
@@ -455,7 +587,7 @@ int conv_plan(ConvPlan* p, const void* xin, int rows, int T, int Cin, int ctx, c
   }
   const int total = a.m_tiles * a.n_tiles;
   p->grid = dim3(std::min(total, sms));
-  p->smem = a.stages * stage_bytes + 1024 + 256;
+  p->smem = (a.slab ? a.na * a.a_slot + a.nb * b_bytes : a.stages * stage_bytes) + 1024 + 256;
   return A8_OK;
 }
 
