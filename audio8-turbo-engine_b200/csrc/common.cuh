@@ -158,6 +158,25 @@ __device__ __forceinline__ uint32_t dsmem_addr(uint32_t local, uint32_t rank) {
 __device__ __forceinline__ void dsmem_st(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
+// the two halves of a cluster barrier, for work between them (all threads of every CTA execute both)
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+// 16 bytes into another CTA's shared memory without waiting for it: the bytes count towards the transaction count of
+// that CTA's mbarrier (both addresses from mapa, 16-byte aligned data)
+__device__ __forceinline__ void dsmem_st_async4(uint32_t addr, uint32_t remote_bar, float a, float b, float c,
+                                                float d) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+      "f"(a), "f"(b), "f"(c), "f"(d), "r"(remote_bar)
+      : "memory");
+}
+// 16 bytes to another CTA's shared memory (addr 16-byte aligned)
+__device__ __forceinline__ void dsmem_st4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
 __device__ __forceinline__ float dsmem_ld(uint32_t addr) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");

@@ -5,10 +5,13 @@
 // byte is read from HBM once per launch. One CTA = 128 weight rows x ntok token rows x a K range:
 //   warp 0 / one lane : TMA producer (128B-swizzled K-major tiles of W and X, a ring of `stages` smem slots)
 //   warp 1 / one lane : MMA issuer (tcgen05.mma kind::f16, fp32 accumulator in TMEM, commit frees a slot)
-//   all 4 warps       : epilogue (tcgen05.ld 32 lanes x 32 columns per warp, staged through smem)
-// Split-K across blockIdx.z writes fp32 partials; the last block of a tile (atomic ticket) adds them in split order
-// (deterministic) and runs the epilogue. Launched with programmatic dependent launch: the weight tiles of the first
-// stages are requested before griddepcontrol.wait, i.e. while the previous kernel is still finishing.
+//   all 16 warps      : epilogue (tcgen05.ld 32 lanes x 32 columns per warp; four 32-column chunks at once, each
+//                       staged transposed through smem and finished by a 128-thread group)
+// K splits of a tile (blockIdx.z) run as one thread-block cluster: each CTA sends its fp32 partial of every token
+// column to the column's owner rank with asynchronous distributed-shared-memory stores (counted by the owner's
+// mbarrier); the owner adds them in split order (deterministic) and runs the epilogue. Launched with programmatic
+// dependent launch: the weight tiles of the first stages are requested before griddepcontrol.wait, i.e. while the
+// previous kernel is still finishing.
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
@@ -24,6 +27,8 @@ constexpr int BK = 64;                  // K elements per stage (128 bytes of bf
 constexpr int TILE_A_BYTES = 128 * BK * 2;
 constexpr int STAGE_PITCH = 132;        // fp32 epilogue staging row pitch (bank-conflict-free float4 reads)
 constexpr int KERNEL_ID_GEMM = 1;
+constexpr int GEMM_PARTS = 4;           // warps per TMEM lane quarter in the epilogue
+constexpr int GEMM_THREADS = 128 * GEMM_PARTS;
 
 struct EpiCtx {
   const GemmArgs* a;
@@ -31,6 +36,18 @@ struct EpiCtx {
 };
 
 // ------------------------------------------------------------------------------------------------ epilogues
+// 8 bf16 (16-byte aligned) -> fp32
+__device__ __forceinline__ void load8_bf16(const __nv_bfloat16* p, float* o) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack_bf16(w[i]);
+    o[2 * i] = f.x;
+    o[2 * i + 1] = f.y;
+  }
+}
+
 // Every epilogue sees one chunk of 32 token columns: stage[j][r] = fp32 result of weight row n0 + r, token m_base + j.
 // Thread t handles token j = t / 4 and the 32 weight rows [32 (t % 4), +32) of the tile.
 template <int KIND>
@@ -52,11 +69,38 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, const float* s
     const __nv_bfloat16* bias = reinterpret_cast<const __nv_bfloat16*>(e.bias);
     __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(a.y) + (size_t)m * a.ldy;
     float o[32];
+    const bool vec = nb + 32 <= a.N;                 // whole segment: 16-byte loads of bias / residual / gamma
+    if (vec && (KIND == A8_EPI_LSRES || bias != nullptr)) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float bx[8];
+        if (bias != nullptr) {
+          load8_bf16(bias + nb + 8 * q, bx);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) bx[k] = 0.f;
+        }
+        if constexpr (KIND == A8_EPI_LSRES) {
+          float rx[8], gx[8];
+          const __nv_bfloat16* res = reinterpret_cast<const __nv_bfloat16*>(e.res) + (size_t)m * e.ldres;
+          load8_bf16(res + nb + 8 * q, rx);
+          load8_bf16(reinterpret_cast<const __nv_bfloat16*>(e.gamma) + nb + 8 * q, gx);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) o[8 * q + k] = rx[k] + bf16r(gx[k] * bf16r(v[8 * q + k] + bx[k]));
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) v[8 * q + k] += bx[k];
+        }
+      }
+    }
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       const int n = nb + i;
       float x = v[i];
-      if (bias != nullptr && n < a.N) x += __bfloat162float(bias[n]);
+      if constexpr (KIND == A8_EPI_LSRES) {
+        if (vec) continue;                           // done above
+      }
+      if (!vec && bias != nullptr && n < a.N) x += __bfloat162float(bias[n]);
       if constexpr (KIND == A8_EPI_BF16) {
         o[i] = x;
       } else if constexpr (KIND == A8_EPI_GELU) {
@@ -148,27 +192,38 @@ __device__ __forceinline__ void epilogue_rope(const GemmArgs& a, const float* st
   const int slot = e.slot != nullptr ? e.slot[m] : m;
   float o[32];
   if (head < e.nq + e.nkv) {
-    const __nv_bfloat16* cs = reinterpret_cast<const __nv_bfloat16*>(e.cos) + (size_t)pos * hd;
-    const __nv_bfloat16* sn = reinterpret_cast<const __nv_bfloat16*>(e.sin) + (size_t)pos * hd;
+    const __nv_bfloat16* cs = reinterpret_cast<const __nv_bfloat16*>(e.cos) + (size_t)pos * hd + d0;
+    const __nv_bfloat16* sn = reinterpret_cast<const __nv_bfloat16*>(e.sin) + (size_t)pos * hd + d0;
     const int pb = n0 + pseg * 32;          // partner rows
     const float sign = d0 < half ? -1.0f : 1.0f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      float x = bf16r(src[i]);
-      float xp = bf16r(psrc[i]);
+    for (int q = 0; q < 4; ++q) {           // 8 dims at a time: one 16-byte load of each table row
+      float c[8], s[8], bx[8], bp[8];
+      load8_bf16(cs + 8 * q, c);
+      load8_bf16(sn + 8 * q, s);
       if (bias != nullptr) {
-        x += __bfloat162float(bias[nb + i]);
-        xp += __bfloat162float(bias[pb + i]);
+        load8_bf16(bias + nb + 8 * q, bx);
+        load8_bf16(bias + pb + 8 * q, bp);
       }
-      const float c = __bfloat162float(cs[d0 + i]), s = __bfloat162float(sn[d0 + i]);
-      o[i] = x * c + sign * xp * s;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int i = 8 * q + k;
+        float x = bf16r(src[i]);
+        float xp = bf16r(psrc[i]);
+        if (bias != nullptr) {
+          x += bx[k];
+          xp += bp[k];
+        }
+        o[i] = x * c[k] + sign * xp * s[k];
+      }
     }
   } else {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      float x = bf16r(src[i]);
-      if (bias != nullptr) x += __bfloat162float(bias[nb + i]);
-      o[i] = x;
+    for (int q = 0; q < 4; ++q) {
+      float bx[8];
+      if (bias != nullptr) load8_bf16(bias + nb + 8 * q, bx);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) o[8 * q + k] = bf16r(src[8 * q + k]) + (bias != nullptr ? bx[k] : 0.f);
     }
   }
   __nv_bfloat16* dst;
@@ -203,7 +258,7 @@ __device__ __forceinline__ void run_epilogue(const GemmArgs& a, const float* sta
 
 // ------------------------------------------------------------------------------------------------ kernel
 template <int KIND>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, const GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -212,16 +267,18 @@ __global__ void __launch_bounds__(128, 1)
   // [pipeline slots][cluster split-K: receive buffer S x w x 128 fp32][reduced slice 32 x STAGE_PITCH][barriers]
   const int ntok32 = (a.ntok + 31) / 32 * 32;
   const int S = a.splits;
-  const int w = (ntok32 + S - 1) / S;                       // token columns each cluster rank reduces
+  const int w = ((ntok32 + S - 1) / S + 3) / 4 * 4;         // token columns each cluster rank reduces
+  const int wp = w % 32 ? w : w + 4;                        // their row pitch in the receive buffer (bank spread)
   const uint32_t pipe_bytes = stages * stage_bytes;
-  const uint32_t recv_bytes = S > 1 ? uint32_t(S * w * 128 * 4) : 0u;
+  const uint32_t recv_bytes = S > 1 ? uint32_t(S * 128 * wp * 4) : 0u;
   const uint32_t slice_bytes = S > 1 ? uint32_t(32 * STAGE_PITCH * 4) : 0u;
   float* recv = reinterpret_cast<float*>(smem + pipe_bytes);
   float* slice = reinterpret_cast<float*>(smem + pipe_bytes + recv_bytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + pipe_bytes + recv_bytes + slice_bytes);
   uint64_t* empty = full + stages;
   uint64_t* accum = empty + stages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* recv_bar = accum + 1;         // split-K: the peers' partials have all landed in recv
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile_n = blockIdx.x, tile_m = blockIdx.y, split = blockIdx.z;
@@ -237,6 +294,7 @@ __global__ void __launch_bounds__(128, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(accum, 1);
+    mbar_init(recv_bar, 1);
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, a.tmem_cols);
@@ -245,6 +303,7 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_launch();
+  if (S > 1) cluster_arrive_relaxed();          // this CTA's recv_bar exists (the peers wait for it before sending)
 
   auto tileA = [&](int s) { return smem + s * stage_bytes; };
   auto tileB = [&](int s) { return smem + s * stage_bytes + TILE_A_BYTES; };
@@ -295,13 +354,48 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();                              // the producer's drain is done before staging reuses the slots
   tc_fence_after();
 
-  float* stage = reinterpret_cast<float*>(smem);  // the pipeline slots are idle now: 32 x STAGE_PITCH fp32
-  const int row = warp * 32 + lane;
-  const uint32_t trow = tmem + (uint32_t(warp * 32) << 16);
+  // Epilogue by all 16 warps. A warp reads the TMEM lanes of its quarter (warp % 4) and the four warps of a quarter
+  // take turns over the 32-column chunks (part = warp / 4), so up to four chunks are in flight; each chunk is staged
+  // transposed in the idle pipeline slots and finished by one 128-thread group (thread t: token t / 4, 32 rows).
+  constexpr int CHUNK_FLOATS = 32 * STAGE_PITCH;
+  const int quarter = warp & 3, part = warp >> 2, gtid = tid & 127;
+  const int row = quarter * 32 + lane;
+  const uint32_t trow = tmem + (uint32_t(quarter * 32) << 16);
   const int nchunk = (a.ntok + 31) / 32;
+  const int par = min(GEMM_PARTS, (int)(pipe_bytes / (CHUNK_FLOATS * 4)));   // chunks staged at once
 
   if (a.splits == 1) {
-    for (int c = 0; c < nchunk; ++c) {
+    for (int c0 = 0; c0 < nchunk; c0 += par) {
+      const int c = c0 + part;
+      float* stage = reinterpret_cast<float*>(smem) + part * CHUNK_FLOATS;
+      if (part < par && c < nchunk) {
+        float v[32];
+        tmem_ld32(trow + c * 32, v);
+        if (!ok) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) stage[i * STAGE_PITCH + row] = v[i];
+      }
+      __syncthreads();
+      if (part < par && c < nchunk) run_epilogue<KIND>(a, stage, n0, m0 + c * 32, m0 + c * 32 + 32, gtid);
+      __syncthreads();
+    }
+  } else {
+    // The K splits of this tile form one cluster (blockIdx.z = rank). Token column col belongs to rank col / w (w a
+    // multiple of 4): every CTA sends its fp32 partial of each column into the owner's receive buffer
+    // recv[rank][row][col - owner w] with asynchronous 16-byte remote stores that count towards the owner's recv_bar,
+    // then each owner waits for its (S - 1) * 128 * w * 4 bytes, adds its columns over the ranks in split order
+    // (deterministic) from its own shared memory and runs the epilogue on them. The receive buffer is not part of the
+    // pipeline slots: a peer may send while this CTA is still in its mainloop.
+    const uint32_t recv_local = smem_u32(recv);
+    const int owners = (ntok32 + w - 1) / w;
+    const bool owner_here = split < owners;
+    const int my_cols = owner_here ? min(w, ntok32 - split * w) : 0;   // the last owner's range may be shorter
+    if (tid == 0 && owner_here) mbar_arrive_expect_tx(recv_bar, uint32_t((S - 1) * 128 * my_cols * 4));
+    cluster_wait();                             // every peer's recv_bar is initialised
+    for (int c = part; c < nchunk; c += GEMM_PARTS) {
       float v[32];
       tmem_ld32(trow + c * 32, v);
       if (!ok) {
@@ -309,41 +403,41 @@ __global__ void __launch_bounds__(128, 1)
         for (int i = 0; i < 32; ++i) v[i] = 0.f;
       }
 #pragma unroll
-      for (int i = 0; i < 32; ++i) stage[i * STAGE_PITCH + row] = v[i];
-      __syncthreads();
-      run_epilogue<KIND>(a, stage, n0, m0 + c * 32, m0 + c * 32 + 32, tid);
-      __syncthreads();
-    }
-  } else {
-    // The K splits of this tile form one cluster (blockIdx.z = rank). Token column col belongs to rank col / w:
-    // every CTA pushes its fp32 partial of each column into the owner's receive buffer recv[rank][col - owner w][row]
-    // with remote stores, then one cluster barrier, then each owner adds its columns over the ranks in split order
-    // (deterministic) from its own shared memory and runs the epilogue on them. The receive buffer is not part of the
-    // pipeline slots: a peer may push while this CTA is still in its mainloop.
-    const uint32_t recv_local = smem_u32(recv);
-    for (int c = 0; c < nchunk; ++c) {
-      float v[32];
-      tmem_ld32(trow + c * 32, v);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int col = c * 32 + i;
+      for (int g = 0; g < 8; ++g) {
+        const int col = c * 32 + g * 4;
         const int owner = col / w;
-        const uint32_t off = uint32_t(((split * w + (col - owner * w)) * 128 + row) * 4);
-        dsmem_st(dsmem_addr(recv_local + off, owner), ok ? v[i] : 0.f);
+        const uint32_t off = uint32_t(((split * 128 + row) * wp + (col - owner * w)) * 4);
+        if (owner == split) {
+          *reinterpret_cast<float4*>(recv + off / 4) = make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+        } else {
+          dsmem_st_async4(dsmem_addr(recv_local + off, owner), dsmem_addr(smem_u32(recv_bar), owner), v[4 * g],
+                          v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+        }
       }
     }
-    cluster_sync();
+    if (owner_here) mbar_wait(recv_bar, 0, ERR_TIMEOUT_OTHER, KERNEL_ID_GEMM);
+    __syncthreads();                            // this CTA's own partial (plain stores) is visible to all its threads
     const int c0 = min(ntok32, split * w), c1 = min(ntok32, c0 + w);
     for (int cc = c0; cc < c1; cc += 32) {                   // the slice buffer and the epilogue take 32 columns
       const int ce = min(c1, cc + 32);
-      for (int col = cc; col < ce; ++col) {
+      for (int col = cc + 4 * part; col < ce; col += 4 * GEMM_PARTS) {
         const int j = col - c0;
-        float s = 0.f;
-        for (int p = 0; p < S; ++p) s += recv[(p * w + j) * 128 + row];
-        slice[(col - cc) * STAGE_PITCH + row] = s;
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int p = 0; p < S; ++p) {
+          const float4 t = *reinterpret_cast<const float4*>(recv + (p * 128 + row) * wp + j);
+          s.x += t.x;
+          s.y += t.y;
+          s.z += t.z;
+          s.w += t.w;
+        }
+        float* sl = slice + (col - cc) * STAGE_PITCH + row;
+        sl[0] = s.x;
+        sl[STAGE_PITCH] = s.y;
+        sl[2 * STAGE_PITCH] = s.z;
+        sl[3 * STAGE_PITCH] = s.w;
       }
       __syncthreads();
-      run_epilogue<KIND>(a, slice, n0, m0 + cc, m0 + ce, tid);
+      if (part == 0) run_epilogue<KIND>(a, slice, n0, m0 + cc, m0 + ce, gtid);
       __syncthreads();
     }
   }
@@ -454,7 +548,7 @@ static bool cluster_fits(int kind, int smem, int S) {
   configure(kind);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1, 1, S);
-  cfg.blockDim = dim3(128);
+  cfg.blockDim = dim3(GEMM_THREADS);
   cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeClusterDimension;
@@ -499,9 +593,10 @@ int gemm_plan(GemmPlan* p, const void* x, int ldx, const void* w, int N, int K, 
   const int ntok32 = (a.ntok + 31) / 32 * 32;
   int smem = 0;
   for (;;) {
-    // cluster split-K: receive buffer (S x w x 128 fp32) + reduced slice beside the pipeline slots
-    const int w = (ntok32 + a.splits - 1) / a.splits;
-    const int reduce_bytes = a.splits > 1 ? a.splits * w * 128 * 4 + 32 * STAGE_PITCH * 4 : 0;
+    // cluster split-K: receive buffer (S x 128 x wp fp32) + reduced slice beside the pipeline slots (as the kernel)
+    const int w = ((ntok32 + a.splits - 1) / a.splits + 3) / 4 * 4;
+    const int wp = w % 32 ? w : w + 4;
+    const int reduce_bytes = a.splits > 1 ? a.splits * 128 * wp * 4 + 32 * STAGE_PITCH * 4 : 0;
     a.stages = std::max(2, std::min(8, (budget - reduce_bytes) / stage_bytes));
     a.stages = std::min(a.stages, std::max(2, a.kb_per_split));
     smem = a.stages * stage_bytes + reduce_bytes + 1024 + 256;
@@ -529,7 +624,7 @@ static cudaError_t launch_kind(const GemmPlan* p, cudaStream_t s, bool pdl) {
   configure(KIND);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = p->grid;
-  cfg.blockDim = dim3(128);
+  cfg.blockDim = dim3(GEMM_THREADS);
   cfg.dynamicSmemBytes = p->smem_bytes;
   cfg.stream = s;
   cudaLaunchAttribute at[2];
