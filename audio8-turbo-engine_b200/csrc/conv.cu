@@ -24,7 +24,8 @@ namespace a8 {
 
 constexpr int KERNEL_ID_CONV = 4;
 constexpr int CONV_EPI_WARPS = 16;
-constexpr int CONV_THREADS = 64 + 32 * CONV_EPI_WARPS;
+constexpr int CONV_THREADS = 96 + 32 * CONV_EPI_WARPS;   // A producer, MMA, B producer, epilogue
+constexpr int CONV_BAR_BYTES = 512;                        // mbarriers + the TMEM address, after the pipeline
 
 struct ConvArgs {
   int rows, T, Cin, N, taps, dil, ctx;
@@ -35,6 +36,7 @@ struct ConvArgs {
   // slab mode (TT = 128, one batch row a unit): the unit's input rows [t0, t0 + R) of one channel block are
   // loaded ONCE (a slab) and every tap reads it at row offset j*dil; weights stream through their own ring
   int slab, R, na, nb;
+  int resident;             // slab mode, one output tile: all taps x cblocks weight tiles (nb of them) stay loaded
   int sub;                  // 128-row sub-tiles a unit (slab mode: 2 share every weight tile; else 1)
   int hb;                   // slab rows a TMA box (a slab of R rows is ceil(R / hb) boxes)
   uint32_t a_slot;          // bytes of one slab slot
@@ -134,14 +136,14 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   const uint32_t stage_bytes = a_bytes + b_bytes;
   // pipeline: `stages` slots of (A, B) -- or, in slab mode, na slab slots then nb weight slots
   const uint32_t pipe_bytes = a.slab ? a.na * a.a_slot + a.nb * b_bytes : stages * stage_bytes;
-  const int nbar = a.slab ? a.na + a.nb : stages;
+  const int nbar = a.slab ? a.na + (a.resident ? 1 : a.nb) : stages;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + pipe_bytes);
   uint64_t* empty = full + nbar;
   uint64_t* tfull = empty + nbar;         // [2] accumulator ready
   uint64_t* tempty = tfull + 2;           // [2] accumulator drained
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   // the epilogue's per-column constants, staged once: bias [N], then alpha and inv [cout] (no global loads per tile)
-  float* s_bias = reinterpret_cast<float*>(smem + pipe_bytes + 256);
+  float* s_bias = reinterpret_cast<float*>(smem + pipe_bytes + CONV_BAR_BYTES);
   float* s_alpha = s_bias + (a.bias != nullptr ? (a.N + 3) / 4 * 4 : 0);
   float* s_inv = s_alpha + (a.cout + 3) / 4 * 4;
 
@@ -182,59 +184,66 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
 
   if (a.slab) {
     // ------------------------------------------------------------------ slab mode
-    // order of use: for each unit, for each channel block c: the slab (A slot), then the taps' weight tiles (B slots)
+    // A (warp 0): for each unit, for each channel block c, the slab of its input rows. B (warp 2): the weight tiles
+    // of (channel block, tap) -- all of them loaded once and kept (a.resident), or streamed through a ring of nb
+    // slots in the order the MMA uses them. The two producers never wait on each other.
     auto slotA = [&](int s) { return smem + s * a.a_slot; };
     auto slotB = [&](int s) { return smem + a.na * a.a_slot + s * b_bytes; };
     uint64_t *fullA = full, *emptyA = empty, *fullB = full + a.na, *emptyB = empty + a.na;
     if (warp == 0 && lane == 0) {
-      const uint64_t pol_w = policy_evict_last(), pol_x = policy_evict_first();
+      const uint64_t pol_x = policy_evict_first();
       const int nbox = (a.R + a.hb - 1) / a.hb;
       const uint32_t box_bytes = a.hb * KC * 2, slab_bytes = nbox * box_bytes;
-      int qa = 0, qb = 0;
+      int qa = 0;
       bool ok = true;
-      // the first unit's first weight tiles do not depend on the previous kernel: issue them before waiting for it
-      const int pre = blockIdx.x < total ? min(a.nb, a.taps) : 0;
-      if (pre > 0) {
-        int b0, t0, n0;
-        coords(blockIdx.x, &b0, &t0, &n0);
-        for (int j = 0; j < pre; ++j) {
-          mbar_arrive_expect_tx(&fullB[j], b_bytes);
-          tma_load_2d(slotB(j), &tmW, &fullB[j], j * a.Cin, n0, pol_w);
-        }
-      }
-      pdl_wait();
+      pdl_wait();                              // the input rows are the previous kernel's output
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
         int b0, t0, n0;
         coords(tile, &b0, &t0, &n0);
-        for (int c = 0; c < cblocks && ok; ++c) {
+        for (int c = 0; c < cblocks; ++c) {
           const int sa = qa % a.na;
           if (!(ok = mbar_wait(&emptyA[sa], ((qa / a.na) & 1) ^ 1, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
           mbar_arrive_expect_tx(&fullA[sa], slab_bytes);
-          for (int x = 0; x < nbox; ++x)       // rows past the end of the input read as zeros (and go unused)
+          for (int x = 0; x < nbox; ++x)         // rows past the end of the input read as zeros (and go unused)
             tma_load_3d(slotA(sa) + x * box_bytes, &tmX, &fullA[sa], c * KC, t0 + x * a.hb, b0, pol_x);
           ++qa;
-          for (int j = 0; j < a.taps; ++j) {
-            if (qb < pre) {                        // issued before the wait
-              ++qb;
-              continue;
-            }
-            const int sb = qb % a.nb;
-            if (!(ok = mbar_wait(&emptyB[sb], ((qb / a.nb) & 1) ^ 1, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
-            mbar_arrive_expect_tx(&fullB[sb], b_bytes);
-            tma_load_2d(slotB(sb), &tmW, &fullB[sb], j * a.Cin + c * KC, n0, pol_w);
-            ++qb;
-          }
         }
       }
       // every load issued has landed before the CTA can exit (also after a timeout)
       for (int i = max(0, qa - a.na); i < qa; ++i)
         mbar_wait(&fullA[i % a.na], (i / a.na) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
-      for (int i = max(0, qb - a.nb); i < qb; ++i)
-        mbar_wait(&fullB[i % a.nb], (i / a.nb) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
+    } else if (warp == 2 && lane == 0) {
+      // weights are never written by a previous kernel: no wait for it
+      const uint64_t pol_w = policy_evict_last();
+      if (a.resident) {                        // one output tile (n0 = 0): every (c, j) tile, once
+        mbar_arrive_expect_tx(&fullB[0], uint32_t(a.nb) * b_bytes);
+        for (int c = 0; c < cblocks; ++c)
+          for (int j = 0; j < a.taps; ++j)
+            tma_load_2d(slotB(c * a.taps + j), &tmW, &fullB[0], j * a.Cin + c * KC, 0, pol_w);
+        mbar_wait(&fullB[0], 0, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
+      } else {
+        int qb = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+          int b0, t0, n0;
+          coords(tile, &b0, &t0, &n0);
+          for (int c = 0; c < cblocks && ok; ++c) {
+            for (int j = 0; j < a.taps; ++j) {
+              const int sb = qb % a.nb;
+              if (!(ok = mbar_wait(&emptyB[sb], ((qb / a.nb) & 1) ^ 1, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
+              mbar_arrive_expect_tx(&fullB[sb], b_bytes);
+              tma_load_2d(slotB(sb), &tmW, &fullB[sb], j * a.Cin + c * KC, n0, pol_w);
+              ++qb;
+            }
+          }
+        }
+        for (int i = max(0, qb - a.nb); i < qb; ++i)
+          mbar_wait(&fullB[i % a.nb], (i / a.nb) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
+      }
     } else if (warp == 1 && lane == 0) {
       const uint32_t idesc = umma_idesc(128, a.ntile, 0);   // fp16 x fp16 -> fp32
       int qa = 0, qb = 0, it = 0;
-      bool ok = true;
+      bool ok = !a.resident || mbar_wait(&fullB[0], 0, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
         const int acc = it & 1, use = it >> 1;
         if (!(ok = mbar_wait(&tempty[acc], (use & 1) ^ 1, ERR_TIMEOUT_ACCUM, KERNEL_ID_CONV))) break;
@@ -243,11 +252,15 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
         for (int c = 0; c < cblocks && ok; ++c) {
           const int sa = qa % a.na;
           if (!(ok = mbar_wait(&fullA[sa], (qa / a.na) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
+          tc_fence_after();
           const uint32_t slab = smem_u32(slotA(sa));
           for (int j = 0; j < a.taps; ++j) {
-            const int sb = qb % a.nb;
-            if (!(ok = mbar_wait(&fullB[sb], (qb / a.nb) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
-            tc_fence_after();
+            int sb = c * a.taps + j;
+            if (!a.resident) {
+              sb = qb % a.nb;
+              if (!(ok = mbar_wait(&fullB[sb], (qb / a.nb) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
+              tc_fence_after();
+            }
             const uint64_t db = KC == 64 ? umma_desc_sw128(slotB(sb)) : umma_desc_sw64(slotB(sb));
             for (int s = 0; s < a.sub; ++s) {    // the sub-tiles share the weight tile
               const uint32_t arow = slab + uint32_t(s * 128 + j * a.dil) * (KC * 2);
@@ -256,8 +269,10 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
 #pragma unroll
               for (int k = 0; k < KC / 16; ++k) umma_f16(d, da + 2 * k, db + 2 * k, idesc, (c | j | k) != 0);
             }
-            umma_commit(&emptyB[sb]);
-            ++qb;
+            if (!a.resident) {
+              umma_commit(&emptyB[sb]);
+              ++qb;
+            }
           }
           umma_commit(&emptyA[sa]);
           ++qa;
@@ -340,15 +355,15 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       }
     }
   }
-  if (warp >= 2) {
+  if (warp >= 3) {
     // ---------------------------------------------------------------- epilogue warps
-    const int ew = warp - 2;                  // 0 .. CONV_EPI_WARPS-1
+    const int ew = warp - 3;                  // 0 .. CONV_EPI_WARPS-1
     const int quarter = warp & 3;             // TMEM lanes [32 quarter, +32) are this warp's
     const int part = ew >> 2;                 // the warps on one quarter split the 16-column chunks round robin
     constexpr int PARTS = CONV_EPI_WARPS / 4;
     const int r = quarter * 32 + lane;        // token row of the tile
     {                                         // weights, not written by the previous kernel: before its end
-      const int et = tid - 64;
+      const int et = tid - 96;
       if (a.bias != nullptr)
         for (int i = et; i < a.N; i += 32 * CONV_EPI_WARPS) s_bias[i] = a.bias[i];
       if (a.alpha != nullptr)
@@ -360,6 +375,20 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
     }
     pdl_wait();                               // outputs may be buffers the previous kernel still reads
     const int nchunk = (a.ntile + 15) / 16;
+    const int W = a.sub * nchunk;             // epilogue items of a unit: (sub-tile, 16-column chunk) pairs
+    auto first_item = [&](int itn) {
+      const int f = part - (itn * W) % PARTS;
+      return f < 0 ? f + PARTS : f;
+    };
+    auto res_load = [&](int tl, int g, uint32_t* q) {   // this thread's residual segment of item g of unit tl
+      int b0, t0, n0;
+      coords(tl, &b0, &t0, &n0);
+      const int bb = b0 + r / a.TT, nb = n0 + (g % nchunk) * 16;
+      if (a.res != nullptr && bb < a.rows && nb + 16 <= a.N)
+        ld_global_v8(a.res + (size_t)bb * a.res_bs + (size_t)(t0 + (g / nchunk) * 128 + r % a.TT) * a.res_ts + nb, q);
+    };
+    uint32_t rc[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // the residual of this warp's next item
+    int rc_tile = -1;                         // the unit whose first item rc already holds
     int it = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
       const int acc = it & 1, use = it >> 1;
@@ -381,21 +410,32 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
           }
         }
       } else {
-        // the unit's (sub-tile, 16-column chunk) pairs, round robin over the warps of this lane quarter
-        for (int f = part; f < a.sub * nchunk; f += PARTS) {
+        // the unit's (sub-tile, 16-column chunk) items, dealt round robin over the warps of this lane quarter with
+        // the deal continuing from tile to tile (a warp left with fewer items of one tile takes more of the next).
+        // Each item's residual (one 32-byte load a thread) is requested while the item before it computes -- the
+        // first item of the next tile's during this tile's last.
+        int f = first_item(it);
+        if (rc_tile != tile && f < W) res_load(tile, f, rc);
+        rc_tile = -1;
+        for (; f < W; f += PARTS) {
+          uint32_t rn[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+          if (f + PARTS < W) {
+            res_load(tile, f + PARTS, rn);
+          } else if (tile + (int)gridDim.x < total && first_item(it + 1) < W) {
+            res_load(tile + gridDim.x, first_item(it + 1), rn);
+            rc_tile = tile + gridDim.x;
+          }
           const int s = f / nchunk, ch = f % nchunk;
           const int t = t0 + s * 128 + r % a.TT;
           const uint32_t trow = tbase + s * a.acc_cols;
           const int nb = n0 + ch * 16;
-          if (nb >= a.N) continue;             // warp-uniform
+          if (nb >= a.N) {                     // warp-uniform
+#pragma unroll
+            for (int i = 0; i < 8; ++i) rc[i] = rn[i];
+            continue;
+          }
           const int nn = min(16, a.N - nb);
           const bool has_res = a.res != nullptr && live && nn == 16;
-          uint4 r0 = make_uint4(0, 0, 0, 0), r1 = r0;
-          if (has_res) {                       // the residual's latency overlaps the TMEM read
-            const uint4* rp = reinterpret_cast<const uint4*>(a.res + (size_t)b * a.res_bs + (size_t)t * a.res_ts + nb);
-            r0 = rp[0];
-            r1 = rp[1];
-          }
           float v[16];
           tmem_ld16(trow + ch * 16, v);
           if (nn == 16) {
@@ -415,10 +455,9 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
               }
             }
             if (has_res) {
-              const uint32_t w[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
 #pragma unroll
               for (int i = 0; i < 8; ++i) {
-                const float2 f = unpack_f16(w[i]);
+                const float2 f = unpack_f16(rc[i]);
                 v[2 * i] += f.x;
                 v[2 * i + 1] += f.y;
               }
@@ -452,17 +491,14 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
               tmem_ld16(trow + ch * 16, v);
               if (live) exact_chunk(a, v, b, t, nb, act, hy, ha);
             }
-            if (live) {
-              if (a.raw != nullptr) {
-                uint4* d = reinterpret_cast<uint4*>(a.raw + (size_t)b * a.raw_bs + (size_t)t * a.raw_ts + nb);
-                d[0] = make_uint4(hy[0], hy[1], hy[2], hy[3]);
-                d[1] = make_uint4(hy[4], hy[5], hy[6], hy[7]);
-              }
+            if (live) {                                      // one full 32-byte sector a thread and output
+              if (a.raw != nullptr) st_global_v8(a.raw + (size_t)b * a.raw_bs + (size_t)t * a.raw_ts + nb, hy);
               if (a.nxt != nullptr) {
-                const uint32_t* o = act ? ha : hy;
-                uint4* d = reinterpret_cast<uint4*>(a.nxt + (size_t)b * a.nxt_bs + a.nxt_off + (size_t)t * a.N + nb);
-                d[0] = make_uint4(o[0], o[1], o[2], o[3]);
-                d[1] = make_uint4(o[4], o[5], o[6], o[7]);
+                __half* d = a.nxt + (size_t)b * a.nxt_bs + a.nxt_off + (size_t)t * a.N + nb;
+                if (act)
+                  st_global_v8(d, ha);
+                else
+                  st_global_v8(d, hy);
               }
             }
           } else if (live) {
@@ -483,6 +519,8 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
               }
             }
           }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) rc[i] = rn[i];
         }
       }
       tc_fence_before();
@@ -549,7 +587,11 @@ int conv_plan(ConvPlan* p, const void* xin, int rows, int T, int Cin, int ctx, c
   a.kb_total = taps * (Cin / a.KC);
   a.acc_cols = a.ntile <= 32 ? 32 : a.ntile <= 64 ? 64 : a.ntile <= 128 ? 128 : 256;
   const int stage_bytes = 128 * a.KC * 2 + a.ntile * a.KC * 2;
-  a.stages = std::max(2, std::min(8, (176 * 1024) / stage_bytes));   // room for the staged column constants
+  // shared memory for the pipeline: what is left of 227 KB after the alignment slack, the barriers and the
+  // epilogue's staged column constants (bias [N], alpha and inv [cout <= N])
+  const int n4 = (N + 3) / 4 * 4;
+  const int budget = 227 * 1024 - 1024 - CONV_BAR_BYTES - 3 * n4 * 4;
+  a.stages = std::max(2, std::min(8, budget / stage_bytes));
   a.cout = N;
   // slab mode: units of one batch row, 128 steps -- or two 128-step sub-tiles sharing each weight tile when T allows
   // and the output tile is at most 128 columns (the accumulator pairs stay double-buffered in 512 TMEM columns;
@@ -564,12 +606,18 @@ int conv_plan(ConvPlan* p, const void* xin, int rows, int T, int Cin, int ctx, c
     a.hb = a.R <= 256 ? a.R : ((a.R + 1) / 2 + 7) / 8 * 8;   // boxes of <= 256 rows, 8-row aligned
     const int nbox = (a.R + a.hb - 1) / a.hb;
     a.a_slot = ((uint32_t)nbox * a.hb * a.KC * 2 + 1023) / 1024 * 1024;
-    a.na = 2;
-    a.nb = std::min(8, (int)((176 * 1024 - a.na * a.a_slot) / b_bytes));
-    if (a.nb < 2) {
-      a.slab = 0;
-      a.sub = 1;
-      return A8_ERR_SIZE;                                    // (not reached with the decoder's shapes)
+    // weights resident when one output tile's (every tap and channel block) fit beside two slab slots; the
+    // rest of the room deepens the slab ring (up to 4). Otherwise two slab slots and a ring of weight tiles.
+    const int wres = taps * (Cin / a.KC) * b_bytes;
+    if (a.n_tiles == 1 && wres + 2 * (int)a.a_slot <= budget) {
+      a.resident = 1;
+      a.nb = taps * (Cin / a.KC);
+      a.na = std::min(4, (budget - wres) / (int)a.a_slot);
+    } else {
+      a.resident = 0;
+      a.na = 2;
+      a.nb = std::min(16, (budget - a.na * (int)a.a_slot) / b_bytes);
+      if (a.nb < 2) return A8_ERR_SIZE;                      // (not reached with the decoder's shapes)
     }
   }
   const CUtensorMapSwizzle sw = a.KC == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
@@ -587,7 +635,7 @@ int conv_plan(ConvPlan* p, const void* xin, int rows, int T, int Cin, int ctx, c
   }
   const int total = a.m_tiles * a.n_tiles;
   p->grid = dim3(std::min(total, sms));
-  p->smem = (a.slab ? a.na * a.a_slot + a.nb * b_bytes : a.stages * stage_bytes) + 1024 + 256;
+  p->smem = (a.slab ? a.na * a.a_slot + a.nb * b_bytes : a.stages * stage_bytes) + 1024 + CONV_BAR_BYTES;
   return A8_OK;
 }
 

@@ -1,9 +1,17 @@
 #!/usr/bin/env python3
 """Benchmark of the Audio8 decode tick on B200 (one JSON line on stdout, rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg1]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg2|cfg1|cfg3|streams]
 
-Workload cfg1 (BASELINE.json configs[1]): the slow-AR decode step alone, bf16, bucket of 64 slots, each slot's KV
+Workload cfg2 (the default): the full tick at 192 rows -- slow AR step, fast AR, streaming
+codec -- replayed from one CUDA graph; value = frames/s, e2e = the same with each tick's inputs copied in from pinned
+host memory and its audio, tokens and frames copied back; roofline = the codec conv with the largest time.
+
+Workloads cfg3 / streams (configs[3], [4] under torchrun): the serving loop (serving.ContinuousBatcher) over an engine of
+1024 slots on a Poisson trace (40 req/s a GPU for 60 s; with N GPUs one global trace at 40N req/s split by
+least-loaded assignment) or on --streams closed-loop users; value = real-time streams a GPU, with P95 RTF and TTFA.
+
+Workload cfg1 (configs[1]): the slow-AR decode step alone, bf16, bucket of 64 slots, each slot's KV
 length drawn uniform in [200, 1500] from seed 1, one new token a slot, the stand-in model's full shapes (24 layers,
 896 wide, GQA 14/2, FFN 4864, semantic head of 4097 rows). A step = input embedding + 24 layers + head + semantic draw
 + state update, replayed from one CUDA graph; every slot's position is restored before each step so the workload is
@@ -133,6 +141,8 @@ def cpu_sample(steps, threads=None):
 def run_reference(args):
     if args.workload == "cfg2":
         return run_reference_cfg2(args)
+    if args.workload in ("cfg3", "streams"):
+        return run_reference_serving(args)
     value, cores, dt = cpu_sample(max(1, args.steps))
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": 0, "ms_per_step": round(1000 * dt / max(1, args.steps), 3),
@@ -141,6 +151,23 @@ def run_reference(args):
             "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port",
                              "sample": f"{args.steps} cfg1 steps (64 rows, KV U[200,1500], 24 layers + head)"},
             "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_serving(args):
+    """The CPU path as a stream count: its full-tick throughput (cfg2 sample) x frame length x 0.7 -- the streams it
+    could keep at RTF 0.7 if its throughput held at any row count (an upper bound; a trace is not replayed on it)."""
+    steps = max(1, min(args.steps, 2))
+    fps, cores, dt = cpu_sample_cfg2(args.cpu_rows, steps)
+    value = fps * (2048 / 44100) * 0.7
+    line = {"impl": "reference", "metric": SERVE_METRIC, "value": round(value, 3), "unit": "streams",
+            "n_gpus": args.gpus, "steps": steps, "warmup": 0, "ms_per_step": round(1000 * dt / steps, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 (bf16 / fp16 rounding points)", "data": "synthetic", "config": serve_dict(args, 1),
+            "cpu_baseline": {"value": round(value, 3), "unit": "streams", "cores": cores, "kind": "port",
+                             "sample": f"{steps} full tick(s) of {args.cpu_rows} rows on the CPU restatement "
+                                       f"({fps:.2f} frames/s), as streams at RTF 0.7"},
+            "e2e": {"value": round(value, 3), "unit": "streams", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -566,13 +593,122 @@ def conv_roofline(eng, L, dev, b, args):
     return roof, res
 
 
+SERVE_METRIC = "real-time streams/GPU at P95 RTF<0.7"
+SERVE_BUCKETS = [1, 2, 4, 6, 8, 12, 16, 20, 24, 28, 32, 40, 48, 56, 64, 72, 80, 88, 96, 104, 112, 120, 128, 144, 160,
+                 176, 192, 224, 256, 288, 320, 384, 448, 512, 576, 640, 704, 768, 832, 896, 960, 1024]
+
+
+def serve_dict(args, world):
+    if args.workload == "streams":
+        w = (f"closed loop: {args.streams} streams a GPU, each asking for its next utterance when one ends, for "
+             f"{args.seconds:g} s")
+    else:
+        w = (f"cfg{3 if world == 1 else 4}: Poisson arrivals at {args.rate * world:g} req/s for {args.seconds:g} s"
+             + (f", assigned to {world} replicas by least-loaded slot count" if world > 1 else ""))
+    return {"workload": w + "; prompts U[20,200] random ids, one of 8 cached voices (150-frame prefixes), output "
+                            "geometric mean 300 frames capped 1024; ragged packed prefill into running ticks, "
+                            f"max_slots {args.slots}",
+            "model": "Audio8 stand-in (seeded random weights, reference shapes)", "parallelism": f"replicas x{world}",
+            "timing": "wall clock, as the reference's serving numbers (RTF = wall time / audio length, TTFA "
+                      "included); the first tick of a row (its silence frame) is not audio"}
+
+
+def run_serving(args, rank, world, local):
+    """BASELINE configs[3] (1 GPU) and [4] (one replica a GPU): the trace through serving.ContinuousBatcher."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__ as G
+    from oracle.standin import StandinConfig, StubTokenizer, build_standin
+    G.build()
+    a8 = G.load_package()
+    import importlib
+    S = importlib.import_module(a8.__name__ + ".serving")
+    torch.cuda.set_device(local)
+    model = build_standin(0, StandinConfig())
+    ncb = int(model.config.num_codebooks)
+    gp = dict(do_sample=True, temperature=0.8, top_k=50, top_p=0.95)
+    t0 = time.perf_counter()
+    eng = a8.FastEngine(model, StubTokenizer(), gp, max_slots=args.slots, max_seq=2048,
+                        buckets=[b for b in SERVE_BUCKETS if b <= args.slots], seq_from_env=False, seed=1234 + rank)
+    del model
+    eng.capture(log=lambda *a: None)
+    t_build = time.perf_counter() - t0
+    if args.workload == "streams":
+        loop = S.ClosedLoop(args.streams, args.seconds, seed=11 + rank, ncb=ncb)
+        reqs, follow, voices = loop.initial, loop.follow, loop.voices
+    else:
+        reqs, voices = S.poisson_trace(args.rate * world, args.seconds, seed=11, ncb=ncb)
+        if world > 1:
+            k = S.assign_least_loaded(reqs, world)
+            reqs = [r for r, kk in zip(reqs, k) if kk == rank]
+        follow = None
+    S.warm_voices(eng, voices)
+    # warm the admission path (first-call host work) on throwaway requests, then start from clean slots
+    warm = [S.Request(rid=-1 - i, arrival=0.0, text=" ".join(["7"] * 20), item=voices[i % len(voices)][1],
+                      key=voices[i % len(voices)][0], cap=4) for i in range(min(64, args.slots))]
+    bat = S.ContinuousBatcher(eng, admit_every=args.admit_every, admit_batch=args.admit_batch,
+                              max_admit=args.max_admit)
+    bat.run(warm)
+    torch.cuda.synchronize()
+    eng.reset_state()
+    if world > 1:
+        dist.barrier()
+    with Clocks(local) as clk:
+        st = bat.run(reqs, follow=follow)
+    err = a8.device_error()
+    assert err[0] == 0, err
+    done = st.finished()
+    mine = {"ttfa": [r.t_first - r.arrival for r in done],
+            "rtf": [(r.t_done - r.arrival) / (r.frames * st.frame_s) for r in done],
+            "frames": sum(r.frames for r in done), "wall": st.wall, "streams": st.busy_time / max(1e-9, st.wall),
+            "ticks": st.ticks, "summary": st.summary(), "launches": None}
+    allr = [mine]
+    if world > 1:
+        allr = [None] * world
+        dist.all_gather_object(allr, mine)
+    if rank != 0:
+        return None
+    ttfa = np.concatenate([np.array(a["ttfa"]) for a in allr]) * 1000
+    rtf = np.concatenate([np.array(a["rtf"]) for a in allr])
+    p95_rtf, p95_ttfa = float(np.percentile(rtf, 95)), float(np.percentile(ttfa, 95))
+    wall = max(a["wall"] for a in allr)
+    streams = sum(a["streams"] for a in allr)
+    ok = p95_rtf < 0.7 and p95_ttfa < 800
+    frames = sum(a["frames"] for a in allr)
+    # closed loop: the offered streams count when P95 RTF < 0.7 and P95 TTFA < 800 ms hold, else 0; open-loop trace:
+    # the time-averaged concurrent streams it sustained (with meets_target saying whether the bars held)
+    value = (args.streams * world if ok else 0.0) if args.workload == "streams" else streams
+    line = {"metric": SERVE_METRIC, "value": round(value, 1), "unit": "streams", "n_gpus": world,
+            "steps": sum(a["ticks"] for a in allr), "warmup": len(warm), "ms_per_step": round(
+                1000 * wall / max(1, max(a["ticks"] for a in allr)), 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (codec convs fp16)",
+            "data": "synthetic", "config": serve_dict(args, world),
+            "meets_target": ok, "mean_streams": round(streams, 1), "rtf_p95": round(p95_rtf, 4), "rtf_p50": round(float(np.percentile(rtf, 50)), 4),
+            "ttfa_ms_p95": round(p95_ttfa, 1), "ttfa_ms_p50": round(float(np.percentile(ttfa, 50)), 1),
+            "frames_per_s": round(frames / wall, 1), "finished": int(len(rtf)),
+            "per_rank": [a["summary"] for a in allr], "build_s": round(t_build, 1), "clocks": clk.summary(),
+            "e2e": {"value": round(value, 1), "unit": "streams", "h2d_bytes_per_step": None,
+                    "d2h_bytes_per_step": eng.B * (8 + 4 * eng.up), "note": "the trace is end to end by itself: "
+                    "prompts in, every tick's tokens and audio read back to pinned host memory"}}
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="cfg2", choices=["cfg1", "cfg2"])
+    ap.add_argument("--workload", default="cfg2", choices=["cfg1", "cfg2", "cfg3", "streams"])
+    ap.add_argument("--rate", type=float, default=40.0, help="cfg3/cfg4 arrivals a GPU (req/s)")
+    ap.add_argument("--seconds", type=float, default=60.0, help="cfg3/cfg4/streams: trace length")
+    ap.add_argument("--streams", type=int, default=512, help="streams: closed-loop users a GPU")
+    ap.add_argument("--slots", type=int, default=1024, help="cfg3/streams: max_slots")
+    ap.add_argument("--admit-every", type=int, default=2, help="admit every N ticks (serve/engine_worker.py default 2)")
+    ap.add_argument("--admit-batch", type=int, default=8, help="or as soon as N wait (reference default 8)")
+    ap.add_argument("--max-admit", type=int, default=64)
     ap.add_argument("--cpu-steps", type=int, default=None, help="CPU baseline sample: steps (cfg1 3, cfg2 2)")
     ap.add_argument("--cpu-rows", type=int, default=64, help="cfg2 CPU baseline sample: rows of the 192")
     ap.add_argument("--no-cpu", action="store_true")
@@ -595,7 +731,8 @@ def main():
         import torch.distributed as dist
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
-    line = (run_ours if args.workload == "cfg1" else run_ours_cfg2)(args, rank, world, local)
+    run = {"cfg1": run_ours, "cfg2": run_ours_cfg2, "cfg3": run_serving, "streams": run_serving}[args.workload]
+    line = run(args, rank, world, local)
     if rank == 0 and line is not None:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -1,0 +1,233 @@
+"""The continuous-batching loop's scheduling logic on the CPU, over a fake engine that follows FastEngine's slot
+semantics (serve/engine_worker.py:1105-1250): lowest free slots, the bucket covering the highest busy slot, the
+first tick of a row dropped (its audio is the silence frame), EOS or the frame cap ending a row, slots reused."""
+import importlib
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import REPO  # noqa: F401
+
+
+@pytest.fixture(scope="module")
+def serving(a8):
+    return importlib.import_module(a8.__name__ + ".serving")
+
+
+class FakeEngine:
+    """B slots; a row consumes EOS on its `eos_at`-th tick after admission (never if 0); audio = tick count."""
+
+    def __init__(self, B=8, buckets=(1, 2, 4, 8), eos=99):
+        self.B, self.eos, self.up, self.sr = B, eos, 4, 4 * 100        # 10 ms frames
+        self.buckets = sorted(buckets)
+        self.tok_in = torch.zeros(B, dtype=torch.int64)
+        self.audio = torch.zeros(B, self.up)
+        self.n = [0] * B
+        self.eos_at = [0] * B
+        self.replays, self.admitted = [], []
+
+    def bucket_for(self, n):
+        return next((b for b in self.buckets if b >= n), self.buckets[-1])
+
+    def admit(self, slots, reqs):
+        out = []
+        for s, r in zip(slots, reqs):
+            if r["text"] == "too long":
+                out.append(-1)
+                continue
+            self.n[s], self.eos_at[s] = 0, int(r["item"])
+            out.append(10)
+        self.admitted.append(list(slots))
+        return out
+
+    def replay(self, b):
+        self.replays.append(b)
+        for s in range(b):
+            self.n[s] += 1
+            self.tok_in[s] = self.eos if self.n[s] == self.eos_at[s] else 7
+            self.audio[s].fill_(self.n[s])
+
+
+class FakeClock:
+    """Wall clock advanced by the loop itself: 1 ms per poll, plus what `sleep` asks for."""
+
+    def __init__(self):
+        self.t = 0.0
+
+    def __call__(self):
+        self.t += 1e-3
+        return self.t
+
+    def sleep(self, d):
+        self.t += d
+
+
+def _req(serving, rid, arrival, cap, eos_at=0, text=None):
+    return serving.Request(rid=rid, arrival=arrival, text=text or f"r{rid}", item=eos_at, key="v", cap=cap)
+
+
+def test_frames_caps_and_eos(serving):
+    fe = FakeEngine()
+    reqs = [_req(serving, 0, 0.0, cap=5), _req(serving, 1, 0.0, cap=50, eos_at=8), _req(serving, 2, 0.0, cap=3)]
+    clk = FakeClock()
+    st = serving.ContinuousBatcher(fe, admit_every=1).run(reqs, clock=clk, sleep=clk.sleep)
+    assert [r.frames for r in reqs] == [5, 7, 3]        # EOS consumed on tick 8: frames of ticks 2..8
+    assert [r.eos for r in reqs] == [False, True, False]
+    assert all(r.t_first is not None and r.t_done >= r.t_first >= r.arrival for r in reqs)
+    assert [r.slot for r in reqs] == [0, 1, 2]
+    assert fe.admitted == [[0, 1, 2]]                     # one packed admission
+    assert st.summary()["finished"] == 3
+    # the bucket always covers the highest busy slot; busy rows shrink as requests end
+    assert max(fe.replays) == 4 and fe.replays[-1] == 2
+
+
+def test_audio_first_tick_dropped(serving):
+    fe = FakeEngine()
+    got = []
+    b = serving.ContinuousBatcher(fe)
+    b.on_audio = lambda r, a: got.append(float(a[0]))
+    clk = FakeClock()
+    b.run([_req(serving, 0, 0.0, cap=4)], clock=clk, sleep=clk.sleep)
+    assert got == [2.0, 3.0, 4.0, 5.0]                    # tick 1 (the silence frame) is not delivered
+
+
+def test_slots_reused_lowest_first(serving):
+    fe = FakeEngine(B=2, buckets=(1, 2))
+    reqs = [_req(serving, i, 0.0, cap=c) for i, c in enumerate((3, 9, 4, 2))]
+    clk = FakeClock()
+    serving.ContinuousBatcher(fe, admit_every=1).run(reqs, clock=clk, sleep=clk.sleep)
+    assert all(r.t_done is not None for r in reqs)
+    assert [r.slot for r in reqs] == [0, 1, 0, 0]         # slot 0 frees first and is taken by each next request
+    assert [r.frames for r in reqs] == [3, 9, 4, 2]
+    # a request never starts before the one it replaces in its slot has ended
+    assert reqs[2].t_admit >= reqs[0].t_done and reqs[3].t_admit >= reqs[2].t_done
+
+
+def test_rejected_prompt_frees_slot(serving):
+    fe = FakeEngine(B=2, buckets=(2,))
+    reqs = [_req(serving, 0, 0.0, cap=3, text="too long"), _req(serving, 1, 0.0, cap=3)]
+    clk = FakeClock()
+    st = serving.ContinuousBatcher(fe).run(reqs, clock=clk, sleep=clk.sleep)
+    assert reqs[0].rejected and reqs[0].t_done is None
+    assert reqs[1].slot == 1 and reqs[1].frames == 3
+    assert st.summary()["rejected"] == 1
+
+
+def test_arrivals_wait_and_admission_cadence(serving):
+    fe = FakeEngine(B=8)
+    reqs = [_req(serving, 0, 0.0, cap=40)] + [_req(serving, i, 0.005 + 1e-4 * i, cap=5) for i in range(1, 4)]
+    clk = FakeClock()
+    serving.ContinuousBatcher(fe, admit_every=4, admit_batch=32).run(reqs, clock=clk, sleep=clk.sleep)
+    assert fe.admitted[0] == [0]
+    # later arrivals join running ticks only every admit_every ticks, batched into one admission
+    assert len(fe.admitted) <= 3 and sorted(s for a in fe.admitted[1:] for s in a) == [1, 2, 3]
+    assert all(r.t_first - r.arrival < 0.05 for r in reqs)
+
+
+def test_idle_gap_sleeps_until_arrival(serving):
+    fe = FakeEngine()
+    reqs = [_req(serving, 0, 0.0, cap=2), _req(serving, 1, 5.0, cap=2)]
+    clk = FakeClock()
+    st = serving.ContinuousBatcher(fe).run(reqs, clock=clk, sleep=clk.sleep)
+    assert reqs[1].t_admit >= 5.0 and st.wall >= 5.0
+    assert st.ticks == 8      # 4 ticks each: silence frame, 2 frames, and one launched before the end is read
+
+
+def test_closed_loop_users(serving):
+    fe = FakeEngine(B=4, buckets=(4,))
+    cl = serving.ClosedLoop(streams=3, seconds=0.5, seed=0, ncb=10, n_voices=2, voice_frames=4, ramp=0.01,
+                            mean_frames=10.0, cap=20)
+    for r in cl.initial:
+        r.item = 0                                        # the fake's EOS knob: never
+    orig = cl.follow
+
+    def follow(r, t):
+        n = orig(r, t)
+        if n is not None:
+            n.item = 0
+        return n
+    clk = FakeClock()
+    st = serving.ContinuousBatcher(fe, admit_every=1).run(cl.initial, follow=follow, clock=clk, sleep=clk.sleep)
+    users = {}
+    for r in st.requests:
+        users.setdefault(r.user, []).append(r)
+    assert sorted(users) == [0, 1, 2]
+    for rs in users.values():
+        for a, b in zip(rs, rs[1:]):
+            assert b.arrival == pytest.approx(a.t_done)   # the next utterance is asked for when one ends
+        assert rs[-1].arrival < 0.5
+    assert all(r.t_done is not None for r in st.requests)
+    s = st.summary()
+    assert 0 < s["mean_streams"] <= 3.0
+
+
+def test_poisson_trace_shape(serving):
+    reqs, voices = serving.poisson_trace(40.0, 60.0, seed=0, ncb=10)
+    assert len(voices) == 8 and all(v.ref_code.shape == (150, 10) for _, v in voices)
+    n = len(reqs)
+    assert 2100 < n < 2700                                # 40 req/s x 60 s
+    gaps = np.diff([r.arrival for r in reqs])
+    assert abs(gaps.mean() - 1 / 40) < 0.003
+    caps = np.array([r.cap for r in reqs])
+    assert caps.max() <= 1024 and caps.min() >= 1 and 270 < caps.mean() < 330
+    nt = np.array([len(r.text.split()) for r in reqs])
+    assert nt.min() >= 20 and nt.max() <= 200
+    assert {r.key for r in reqs} <= {k for k, _ in voices}
+    again, _ = serving.poisson_trace(40.0, 60.0, seed=0, ncb=10)
+    assert [(r.arrival, r.cap, r.text) for r in again] == [(r.arrival, r.cap, r.text) for r in reqs]
+
+
+def test_least_loaded_assignment(serving):
+    reqs, _ = serving.poisson_trace(320.0, 5.0, seed=3, ncb=10)
+    k = serving.assign_least_loaded(reqs, 8)
+    assert len(k) == len(reqs) and set(k) == set(range(8))
+    # each request went to a replica with the fewest (estimated) streams in flight at its arrival
+    ends = [[] for _ in range(8)]
+    for r, kk in zip(reqs, k):
+        live = [sum(e > r.arrival for e in h) for h in ends]
+        assert live[kk] == min(live)
+        ends[kk].append(r.arrival + r.cap * serving.FRAME_S * 0.5)
+    frames = np.bincount(k, weights=[r.cap for r in reqs], minlength=8)
+    assert frames.max() - frames.min() <= 0.2 * frames.mean()
+    # first arrivals fan out over the replicas in index order
+    first = sorted(range(len(reqs)), key=lambda i: reqs[i].arrival)[:8]
+    assert [k[i] for i in first] == list(range(8))
+    assert serving.assign_least_loaded(reqs, 8) == k      # deterministic: every rank computes the same split
+
+
+def _assign_worker(rank, world, port, out):
+    import torch.distributed as dist
+    import importlib as il
+    from __graft_entry__ import load_package
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    serving = il.import_module(load_package().__name__ + ".serving")
+    reqs, _ = serving.poisson_trace(80.0, 3.0, seed=5, ncb=10)
+    k = serving.assign_least_loaded(reqs, world)
+    mine = [r.rid for r, kk in zip(reqs, k) if kk == rank]
+    gathered = [None] * world
+    dist.all_gather_object(gathered, mine)
+    if rank == 0:
+        out.put((gathered, [r.rid for r in reqs]))
+    dist.destroy_process_group()
+
+
+def test_replica_split_two_ranks():
+    """Two gloo ranks each take their share of one global trace: disjoint, and together the whole trace."""
+    import socket
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    ps = [ctx.Process(target=_assign_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(120)
+    assert all(p.exitcode == 0 for p in ps)
+    gathered, rids = q.get()
+    assert not set(gathered[0]) & set(gathered[1])
+    assert sorted(gathered[0] + gathered[1]) == sorted(rids)
+    assert abs(len(gathered[0]) - len(gathered[1])) <= 0.1 * len(rids)
