@@ -15,6 +15,8 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
+#include <unordered_map>
 
 #include "common.cuh"
 #include "gemm.cuh"
@@ -379,7 +381,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int i = 0; i < 32; ++i) stage[i * STAGE_PITCH + row] = v[i];
       }
       __syncthreads();
-      if (part < par && c < nchunk) run_epilogue<KIND>(a, stage, n0, m0 + c * 32, m0 + c * 32 + 32, gtid);
+      // (a tile's last chunk may reach past its ntok columns into the next tile's tokens: those are not written)
+      if (part < par && c < nchunk)
+        run_epilogue<KIND>(a, stage, n0, m0 + c * 32, min(m0 + c * 32 + 32, m0 + a.ntok), gtid);
       __syncthreads();
     }
   } else {
@@ -437,7 +441,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         sl[3 * STAGE_PITCH] = s.w;
       }
       __syncthreads();
-      if (part == 0) run_epilogue<KIND>(a, slice, n0, m0 + cc, m0 + ce, gtid);
+      if (part == 0) run_epilogue<KIND>(a, slice, n0, m0 + cc, min(m0 + ce, m0 + a.ntok), gtid);
       __syncthreads();
     }
   }
@@ -501,23 +505,6 @@ static int pick_ntok(int M) {
   return std::max(16, (per + 15) / 16 * 16);
 }
 
-static void shape(int N, int K, int M, int splits_req, int* ntok, int* n_tiles, int* tok_tiles, int* kb_total,
-                  int* kb_per_split, int* splits) {
-  *ntok = pick_ntok(M);
-  *n_tiles = (N + 127) / 128;
-  *tok_tiles = (M + *ntok - 1) / *ntok;
-  *kb_total = (K + BK - 1) / BK;
-  int s = splits_req;
-  if (s <= 0) {
-    const int tiles = *n_tiles * *tok_tiles;
-    s = tiles >= 148 ? 1 : std::max(1, 148 / tiles);
-    s = std::min(s, std::max(1, *kb_total / 2));   // at least two K blocks per split
-  }
-  s = std::max(1, std::min(std::min(s, *kb_total), 16));   // the splits of a tile are one cluster (<= 16 CTAs)
-  *kb_per_split = (*kb_total + s - 1) / s;
-  *splits = (*kb_total + *kb_per_split - 1) / *kb_per_split;
-}
-
 static const void* gemm_fn(int kind) {
   switch (kind) {
     case A8_EPI_BF16: return (const void*)k_gemm<A8_EPI_BF16>;
@@ -537,14 +524,16 @@ static void configure(int kind) {
   done[kind] = true;
 }
 
-// Whether a cluster of S CTAs with this shared memory can be resident at all.
-static bool cluster_fits(int kind, int smem, int S) {
-  static long long cache_key[64];
-  static bool cache_val[64];
-  static int n_cache = 0;
+// How many clusters of S CTAs with this shared memory can be resident at once (0: none).
+static int max_clusters(int kind, int smem, int S) {
+  static std::mutex mu;
+  static std::unordered_map<long long, int> cache;
   const long long key = ((long long)kind << 40) | ((long long)smem << 8) | S;
-  for (int i = 0; i < n_cache; ++i)
-    if (cache_key[i] == key) return cache_val[i];
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto f = cache.find(key);
+    if (f != cache.end()) return f->second;
+  }
   configure(kind);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1, 1, S);
@@ -558,14 +547,99 @@ static bool cluster_fits(int kind, int smem, int S) {
   cfg.attrs = at;
   cfg.numAttrs = 1;
   int n = 0;
-  const bool ok = cudaOccupancyMaxActiveClusters(&n, gemm_fn(kind), &cfg) == cudaSuccess && n > 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_fn(kind), &cfg) != cudaSuccess) n = 0;
   cudaGetLastError();
-  if (n_cache < 64) {
-    cache_key[n_cache] = key;
-    cache_val[n_cache++] = ok;
-  }
-  return ok;
+  std::lock_guard<std::mutex> g(mu);
+  cache[key] = n;
+  return n;
 }
+
+static int num_sms() {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+  }
+  return sms;
+}
+
+// Shared memory of a (ntok, splits) configuration: pipeline slots, and for split-K the receive buffer of
+// S x 128 x wp fp32 plus the reduced slice (as the kernel lays them out). Returns the stage count, or 0 if it does
+// not fit in 227 KB.
+static int size_config(int ntok, int S, int kb_per_split, int* smem) {
+  const int stage_bytes = TILE_A_BYTES + ntok * BK * 2;
+  const int ntok32 = (ntok + 31) / 32 * 32;
+  const int w = ((ntok32 + S - 1) / S + 3) / 4 * 4;
+  const int wp = w % 32 ? w : w + 4;
+  const int reduce_bytes = S > 1 ? S * 128 * wp * 4 + 32 * STAGE_PITCH * 4 : 0;
+  int stages = std::max(2, std::min(8, (200 * 1024 - reduce_bytes) / stage_bytes));
+  stages = std::min(stages, std::max(2, kb_per_split));
+  *smem = stages * stage_bytes + reduce_bytes + 1024 + 256;
+  return *smem <= 227 * 1024 ? stages : 0;
+}
+
+// Token tile and K splits of Y[M, N] = X[M, K] . W[N, K]^T. An explicit split count keeps the token tile of at most
+// 256 balanced rows; otherwise every (token tile 32..256, splits 1..16) is scored by a launch-time model fitted to
+// measured times of the tick's GEMM shapes on B200 -- waves of resident CTAs (or clusters) x (per K block cost
+// growing with the tile + a fixed cost), plus the split-K exchange -- and the cheapest is kept (cached per shape).
+static void choose(int kind, int N, int K, int M, int splits_req, int* ntok, int* splits) {
+  const int kb_total = (K + BK - 1) / BK;
+  if (splits_req > 0) {
+    *ntok = pick_ntok(M);
+    *splits = std::max(1, std::min(std::min(splits_req, kb_total), 16));
+    return;
+  }
+  static std::mutex mu;
+  static std::unordered_map<long long, long long> cache;
+  const long long key = ((long long)kind << 56) | ((long long)N << 36) | ((long long)K << 18) | M;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto f = cache.find(key);
+    if (f != cache.end()) {
+      *ntok = int(f->second >> 8);
+      *splits = int(f->second & 0xFF);
+      return;
+    }
+  }
+  const int n_tiles = (N + 127) / 128, sms = num_sms();
+  double best = 1e30;
+  // below 128 token rows (weight-bound decode steps): the balanced tile, and splits filling the SMs with at least
+  // two K blocks each
+  int bt = pick_ntok(M), bs = 1;
+  {
+    const int tiles = n_tiles * ((M + bt - 1) / bt);
+    bs = tiles >= sms ? 1 : std::max(1, sms / tiles);
+    bs = std::max(1, std::min(std::min(bs, std::max(1, kb_total / 2)), 16));
+  }
+  for (int nt = 32; nt <= 256 && M >= 128; nt += 16) {
+    const int tt = (M + nt - 1) / nt;
+    const int per = std::max(16, ((M + tt - 1) / tt + 15) / 16 * 16);
+    if (per != nt) continue;                  // (the balanced tile of another candidate)
+    const int tiles = n_tiles * tt;
+    for (int s = 1; s <= std::min(16, kb_total); ++s) {
+      const int kps = (kb_total + s - 1) / s, S = (kb_total + kps - 1) / kps;
+      if (S != s) continue;
+      int smem = 0;
+      if (size_config(per, S, kps, &smem) == 0) continue;
+      const int cap = S == 1 ? sms : max_clusters(kind, smem, S);
+      if (cap <= 0) continue;
+      const int waves = (tiles + cap - 1) / cap;
+      const double t = waves * (kps * (0.2 + 0.3 * per / 128.0) + 3.0) + (S > 1 ? 1.0 + 0.4 * S * per / 128.0 : 0.0);
+      if (t < best - 1e-9) {
+        best = t;
+        bt = per;
+        bs = S;
+      }
+    }
+  }
+  *ntok = bt;
+  *splits = bs;
+  std::lock_guard<std::mutex> g(mu);
+  cache[key] = ((long long)bt << 8) | bs;
+}
+
+static bool cluster_fits(int kind, int smem, int S) { return max_clusters(kind, smem, S) > 0; }
 
 int gemm_plan(GemmPlan* p, const void* x, int ldx, const void* w, int N, int K, int M, void* y, int ldy,
               const A8Epilogue* epi, int splits) {
@@ -580,7 +654,12 @@ int gemm_plan(GemmPlan* p, const void* x, int ldx, const void* w, int N, int K, 
     return A8_ERR_ARG;
   if (epi->kind == A8_EPI_LSRES && (epi->res == nullptr || epi->gamma == nullptr)) return A8_ERR_ARG;
   GemmArgs& a = p->args;
-  shape(N, K, M, splits, &a.ntok, &a.n_tiles, &a.tok_tiles, &a.kb_total, &a.kb_per_split, &a.splits);
+  choose(epi->kind, N, K, M, splits, &a.ntok, &a.splits);
+  a.n_tiles = (N + 127) / 128;
+  a.tok_tiles = (M + a.ntok - 1) / a.ntok;
+  a.kb_total = (K + BK - 1) / BK;
+  a.kb_per_split = (a.kb_total + a.splits - 1) / a.splits;
+  a.splits = (a.kb_total + a.kb_per_split - 1) / a.kb_per_split;
   a.N = N;
   a.K = K;
   a.M = M;

@@ -54,7 +54,11 @@ def rnd(g, *shape, scale=1.0):
 
 @pytest.mark.parametrize("M,N,K,splits", [(1, 1152, 896, 0), (3, 896, 896, 1), (17, 896, 4864, 0),
                                           (64, 4160, 896, 0), (192, 9728, 896, 0), (300, 896, 4864, 0),
-                                          (64, 896, 4864, 5), (2048, 1024, 1024, 0), (130, 4097, 896, 3)])
+                                          (64, 896, 4864, 5), (2048, 1024, 1024, 0), (130, 4097, 896, 3),
+                                          # several token tiles whose width is not a multiple of 32 (a tile's last
+                                          # 32-column chunk reaches into the next tile's tokens)
+                                          (280, 896, 896, 2), (280, 896, 4864, 0), (223, 1152, 896, 0),
+                                          (1000, 896, 896, 0), (1024, 4097, 896, 0), (720, 896, 4864, 0)])
 def test_gemm_bf16(L, ws, M, N, K, splits):
     g = torch.Generator().manual_seed(M * 7 + N)
     x, w = rnd(g, M, K), rnd(g, N, K, scale=K ** -0.5)
@@ -95,7 +99,7 @@ def test_gemm_bias_gelu_lsres_f32(L, ws):
     assert bool((lg[:, N2:] == 7.0).all())                       # nothing written past N
 
 
-@pytest.mark.parametrize("M", [1, 64, 200])
+@pytest.mark.parametrize("M", [1, 64, 200, 223, 450])
 def test_gemm_silu(L, ws, M):
     from audio8_b200.engine import interleave_w13
     g = torch.Generator().manual_seed(M)
