@@ -595,7 +595,8 @@ def conv_roofline(eng, L, dev, b, args):
 
 SERVE_METRIC = "real-time streams/GPU at P95 RTF<0.7"
 SERVE_BUCKETS = [1, 2, 4, 6, 8, 12, 16, 20, 24, 28, 32, 40, 48, 56, 64, 72, 80, 88, 96, 104, 112, 120, 128, 144, 160,
-                 176, 192, 224, 256, 288, 320, 384, 448, 512, 576, 640, 704, 768, 832, 896, 960, 1024]
+                 176, 192, 224, 256, 288, 320, 384, 448, 512, 576, 640, 704, 768, 832, 896, 960, 1024, 1088, 1152,
+                 1216, 1280, 1408, 1536]
 
 
 def serve_dict(args, world):
@@ -695,6 +696,68 @@ def run_serving(args, rank, world, local):
     return line
 
 
+def cfg2_engine(rank=0):
+    """The cfg2 workload's engine and state (as run_ours_cfg2 sets it up); returns (eng, step) with step() one tick."""
+    import torch
+
+    import __graft_entry__ as G
+    from oracle.standin import StandinConfig, StubTokenizer, build_standin
+    G.build()
+    a8 = G.load_package()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    model = build_standin(0, StandinConfig())
+    gp = dict(do_sample=True, temperature=0.8, top_k=50, top_p=0.95)
+    b = B_CFG2
+    eng = a8.FastEngine(model, StubTokenizer(), gp, max_slots=b, max_seq=2048, buckets=[b], seq_from_env=False,
+                        seed=1234 + rank)
+    del model
+    lens = cfg2_lengths()
+    g = torch.Generator(device=dev).manual_seed(3 + rank)
+    for t in (eng.slow.kc, eng.slow.vc, eng.voc.post.kc, eng.voc.post.vc):
+        t.normal_(generator=g)
+    eng.voc.pos.fill_(1000)
+    cpos0 = (lens - 1).to(torch.int32).to(dev)
+    eng.cpos[:b].copy_(cpos0)
+    eng.tok[:b].copy_((eng.sb + torch.randint(0, 4096, (b,), generator=g, device=dev)).long())
+    eng.frame_prev.copy_(torch.randint(0, 4096, (b, eng.ncg), generator=g, device=dev))
+    eng.hid[:b].normal_(generator=g)
+    eng.nstep[:b].fill_(5)
+
+    def step():
+        eng.cpos[:b].copy_(cpos0)
+        eng.tick(b)
+    return a8, eng, step
+
+
+def run_profile(args):
+    """One eager cfg2 tick (after two warm-up ticks), or one decoder conv launch at 192 rows, inside
+    cudaProfilerStart/Stop -- the region an `ncu --profile-from-start off` capture sees."""
+    import ctypes as C
+
+    import torch
+    a8, eng, step = cfg2_engine()
+    L = a8._lib
+    what = args.profile
+    if what == "tick":
+        fn = step
+    elif what.startswith("conv:"):
+        i = int(what.split(":")[1])
+        run = eng.voc.conv_run(i, B_CFG2)
+        fn = lambda: L.call("a8_conv", C.byref(run), L.stream_handle())
+    else:
+        raise SystemExit(f"--profile {what}: expected tick or conv:I")
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    fn()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    err = a8.device_error()
+    assert err[0] == 0, err
+    print(json.dumps({"profile": what, "ok": True}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -712,7 +775,12 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=None, help="CPU baseline sample: steps (cfg1 3, cfg2 2)")
     ap.add_argument("--cpu-rows", type=int, default=64, help="cfg2 CPU baseline sample: rows of the 192")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile", default=None, metavar="tick|conv:I|gemm",
+                    help="no timing: run one eager cfg2 tick (or decoder conv I alone at 192 rows) between "
+                         "cudaProfilerStart/Stop, for ncu --profile-from-start off")
     args = ap.parse_args()
+    if args.profile:
+        return run_profile(args)
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
