@@ -29,9 +29,16 @@ __global__ void k_rmsnorm(const __nv_bfloat16* __restrict__ x, int ldx, __nv_bfl
                           const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y, int ldy, int rows, int N,
                           float eps) {
   pdl_launch();
-  pdl_wait();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  // the weight (never written by a previous kernel) is read before waiting for that kernel
+  float wv[MAXV][8];
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int c = (lane + 32 * i) * 8;
+    if (c < N) ld8(w + c, wv[i]);
+  }
+  pdl_wait();
   if (row >= rows) return;
   const int nv = N >> 3;
   float v[MAXV][8];
@@ -59,10 +66,9 @@ __global__ void k_rmsnorm(const __nv_bfloat16* __restrict__ x, int ldx, __nv_bfl
   for (int i = 0; i < MAXV; ++i) {
     const int c = (lane + 32 * i) * 8;
     if (c < N) {
-      float wv[8], o[8];
-      ld8(w + c, wv);
+      float o[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) o[k] = wv[k] * bf16r(v[i][k] * rs);
+      for (int k = 0; k < 8; ++k) o[k] = wv[i][k] * bf16r(v[i][k] * rs);
       st8(y + (size_t)row * ldy + c, o);
     }
   }

@@ -222,19 +222,41 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const SampleArgs a) {
     for (int shift = 24; shift >= 0; shift -= 8) {
       for (int b = tid; b < 256; b += SAMPLE_THREADS) hist[b] = 0;
       __syncthreads();
-      for (int i = tid; i < V; i += SAMPLE_THREADS) {
-        const uint32_t key = fkey(s_x[i]);
-        if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1);
+      // logits crowd into few bins of the high bytes: lanes of a warp with the same bin add once, together
+      for (int it = 0; it < (V + SAMPLE_THREADS - 1) / SAMPLE_THREADS; ++it) {
+        const int i = it * SAMPLE_THREADS + tid;
+        const uint32_t key = i < V ? fkey(s_x[i]) : 0u;
+        const int bin = (i < V && (key & mask) == prefix) ? int((key >> shift) & 255) : -1;
+        const unsigned peers = __match_any_sync(0xffffffffu, bin);
+        if (bin >= 0 && (tid & 31) == __ffs(peers) - 1) atomicAdd(&hist[bin], __popc(peers));
       }
       __syncthreads();
-      if (tid == 0) {
-        int acc = 0, b = 255;
-        for (; b > 0; --b) {
-          if (acc + hist[b] >= remain) break;
-          acc += hist[b];
+      // the bin holding the remain-th largest key, scanning from bin 255 down: warp 0, lane l owns bins
+      // 255 - 8l .. 248 - 8l; a warp prefix sum of the lane totals finds the one lane whose bins reach `remain`,
+      // which walks its 8 (matching elements always number at least `remain`, so exactly one lane does)
+      if (tid < 32) {
+        int c[8], loc = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          c[q] = hist[255 - (tid * 8 + q)];
+          loc += c[q];
         }
-        s_sel[0] = b;
-        s_sel[1] = acc;
+        int inc = loc;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, inc, o);
+          if (tid >= o) inc += y;
+        }
+        const int pre = inc - loc;
+        if (pre < remain && remain <= inc) {
+          int acc = pre, q = 0;
+          for (; q < 7; ++q) {
+            if (acc + c[q] >= remain) break;
+            acc += c[q];
+          }
+          s_sel[0] = 255 - (tid * 8 + q);
+          s_sel[1] = acc;
+        }
       }
       __syncthreads();
       prefix |= uint32_t(s_sel[0]) << shift;

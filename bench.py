@@ -566,14 +566,17 @@ def conv_roofline(eng, L, dev, b, args):
     _, tf, kind = _peaks()
     voc = eng.voc
     flops = conv_flops(voc, b)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    # L2 flushed between launches by reading 256 MB (a read leaves no dirty lines whose write-back would be charged to
+    # the timed launch)
+    flush = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+    fsum = torch.empty((), device=dev)
     reps = max(3, min(10, args.steps))
     res = []
     for i, (c, T, *_) in enumerate(voc.ops):
         run = voc.conv_run(i, b)
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps + 2)]
         for k, (a, z) in enumerate(ev):
-            flush.zero_()
+            torch.sum(flush, dim=0, out=fsum)
             a.record()
             L.call("a8_conv", C.byref(run), L.stream_handle())
             z.record()
