@@ -598,8 +598,8 @@ def conv_roofline(eng, L, dev, b, args):
 
 SERVE_METRIC = "real-time streams/GPU at P95 RTF<0.7"
 SERVE_BUCKETS = [1, 2, 4, 6, 8, 12, 16, 20, 24, 28, 32, 40, 48, 56, 64, 72, 80, 88, 96, 104, 112, 120, 128, 144, 160,
-                 176, 192, 224, 256, 288, 320, 384, 448, 512, 576, 640, 704, 768, 832, 896, 960, 1024, 1088, 1152,
-                 1216, 1280, 1408, 1536]
+                 176, 192, 224, 256, 288, 320, 384, 448, 512, 576, 640, 704, 768, 832, 896, 960, 992, 1024, 1056, 1088,
+                 1120, 1152, 1184, 1216, 1248, 1280, 1408, 1536]
 
 
 def serve_dict(args, world):
