@@ -801,7 +801,7 @@ def main():
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
     run = {"cfg1": run_ours, "cfg2": run_ours_cfg2, "cfg3": run_serving, "streams": run_serving}[args.workload]
     line = run(args, rank, world, local)
     if rank == 0 and line is not None:
