@@ -1,6 +1,6 @@
 // Per-row sampling with the engine's state updates fused in (serve/fast_engine.py:141-172, :719-769, :820-835).
 //
-// One block of 256 threads per row. The draw follows the checkpoint's sampler step for step:
+// One block of 512 threads per row. The draw follows the checkpoint's sampler step for step:
 //   top-k of the logits (ties: lower index first), each candidate's cumulative probability under the UNTEMPERED
 //   softmax of ALL logits, drop candidates whose cumulative probability passes top_p (the best always stays),
 //   softmax(v / temperature), exponential race argmax(p_i / E_i), E_i ~ Exp(1).
@@ -12,7 +12,7 @@
 
 namespace a8 {
 
-constexpr int SAMPLE_THREADS = 256;
+constexpr int SAMPLE_THREADS = 512;
 constexpr int KERNEL_ID_SAMPLE = 3;
 
 enum SampleMode { SM_CODEBOOK = 0, SM_SEMANTIC = 1, SM_PREFILL = 2, SM_PLAIN = 3 };
