@@ -6,8 +6,9 @@ wait, or when nothing runs) they are admitted into the lowest free slots in ONE 
 engine_worker.py:1105-1140); then the tick of the bucket covering the highest busy slot is replayed
 (``FastEngine.replay(fe.bucket_for(busy[-1] + 1))``, engine_worker.py:1168-1172) and its consumed tokens and audio are
 copied to pinned host buffers asynchronously and read one tick later (engine_worker.py:1180-1215). The vocoder runs
-one frame behind the AR: a row's first tick yields the audio of its silence frame, which is dropped. A row ends on EOS
-or at its frame cap, and its slot is free for the next admission.
+one frame behind the AR: a row's first tick yields the audio of its silence frame, which is dropped. Frames go out as
+chunks of 1, 2, 4, then 6 frames (the worker's ramp), the rest when the row ends; `pcm16` is the worker's int16
+conversion. A row ends on EOS or at its frame cap, and its slot is free for the next admission.
 
 Timing is wall clock, as the reference's serving numbers (README "Results": RTF = wall time / audio duration, TTFA
 included): TTFA = first audio frame on the host - arrival; RTF = (last frame on the host - arrival) / audio length.
@@ -48,6 +49,9 @@ class Request:
     t_done: Optional[float] = None
     eos: bool = False
     rejected: bool = False
+    pend: list = field(default_factory=list)   # frames not yet emitted as a chunk
+    target: int = 0                            # frames the next chunk waits for
+    chunks: int = 0
 
     def as_admit(self):
         return dict(text=self.text, item=self.item, key=self.key)
@@ -102,8 +106,12 @@ class ContinuousBatcher:
     admit(slots, reqs) -> prompt lengths (-1: rejected) and replay(b)."""
 
     def __init__(self, engine, admit_every: int = 2, admit_batch: int = 8, max_admit: int = 64, nbuf: int = 4,
-                 copy_audio: bool = True):
+                 copy_audio: bool = True, first_chunk: int = 1, chunk_frames: int = 6):
         self.fe = engine
+        # streamed chunks (engine_worker.py:696-697, :1246-1248): the first after `first_chunk` frames (the
+        # reference's TTS_FIRST_CHUNK_FRAMES), then doubling up to `chunk_frames` (TTS_FRAMES_PER_CHUNK); the rest
+        # when the row ends
+        self.first_chunk, self.chunk_frames = max(1, first_chunk), max(1, chunk_frames)
         self.admit_every, self.admit_batch, self.max_admit = admit_every, admit_batch, max_admit
         self.nbuf = max(2, nbuf)
         self.copy_audio = copy_audio
@@ -114,6 +122,8 @@ class ContinuousBatcher:
         self.aud_h = pin(torch.empty(self.nbuf, B, engine.up, dtype=torch.float32)) if copy_audio else None
         self.events = [torch.cuda.Event() if cuda else _HostEvent() for _ in range(self.nbuf)]
         self.on_audio: Optional[Callable[[Request, torch.Tensor], None]] = None
+        # on_chunk(request, pcm fp32 [n * up] as numpy, final): a chunk of consecutive frames, as the worker emits
+        self.on_chunk: Optional[Callable[[Request, np.ndarray, bool], None]] = None
 
     def run(self, requests: List[Request], follow: Optional[Callable[[Request, float], Optional[Request]]] = None,
             clock=time.perf_counter, sleep=time.sleep) -> RunStats:
@@ -187,9 +197,19 @@ class ContinuousBatcher:
                             r.t_first = t
                         if self.on_audio is not None:
                             self.on_audio(r, self.aud_h[j, s])
+                        if self.on_chunk is not None:
+                            r.pend.append(self.aud_h[j, s].numpy().copy())
                     else:
                         r.started = True                      # the first tick decodes the silence frame
-                    if toks[s] == eos or r.frames >= r.cap:
+                        r.target = self.first_chunk
+                    end = toks[s] == eos or r.frames >= r.cap
+                    if self.on_chunk is not None and r.pend and (end or len(r.pend) >= r.target):
+                        self.on_chunk(r, np.concatenate(r.pend), end)
+                        r.pend, r.chunks = [], r.chunks + 1
+                        r.target = min(self.chunk_frames, r.target * 2)
+                    elif self.on_chunk is not None and end:
+                        self.on_chunk(r, np.zeros(0, np.float32), True)
+                    if end:
                         r.eos = toks[s] == eos
                         r.t_done = t
                         del rows[s]
@@ -204,6 +224,11 @@ class ContinuousBatcher:
 
 
 # ------------------------------------------------------------------------------------------------ traces
+def pcm16(y: np.ndarray) -> bytes:
+    """fp32 PCM in [-1, 1] to little-endian int16 bytes, as the worker sends it (engine_worker.py:423-424)."""
+    return (np.clip(y, -1.0, 1.0) * 32767.0).astype("<i2").tobytes()
+
+
 def voice_items(n_voices: int, frames: int, ncb: int, seed: int):
     """n_voices cached voices, each a reference of `frames` uniform-random code frames and a short transcript."""
     g = torch.Generator().manual_seed(seed)

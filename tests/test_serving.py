@@ -231,3 +231,22 @@ def test_replica_split_two_ranks():
     assert not set(gathered[0]) & set(gathered[1])
     assert sorted(gathered[0] + gathered[1]) == sorted(rids)
     assert abs(len(gathered[0]) - len(gathered[1])) <= 0.1 * len(rids)
+
+
+def test_chunks_ramp_and_final(serving):
+    """Chunks of 1, 2, 4, 6, 6, ... frames, the rest at the end (the worker's ramp), concatenating to every frame."""
+    fe = FakeEngine()
+    got = []
+    b = serving.ContinuousBatcher(fe, first_chunk=1, chunk_frames=6)
+    b.on_chunk = lambda r, y, final: got.append((len(y) // fe.up, final, y[::fe.up].tolist()))
+    clk = FakeClock()
+    b.run([_req(serving, 0, 0.0, cap=21)], clock=clk, sleep=clk.sleep)
+    assert [n for n, _, _ in got] == [1, 2, 4, 6, 6, 2]
+    assert [f for _, f, _ in got] == [False] * 5 + [True]
+    assert [v for _, _, vs in got for v in vs] == [float(i) for i in range(2, 23)]   # ticks 2..22, in order
+
+
+def test_pcm16(serving):
+    y = np.array([-2.0, -1.0, -0.5, 0.0, 0.5, 1.0, 3.0], dtype=np.float32)
+    out = np.frombuffer(serving.pcm16(y), dtype="<i2")
+    assert out.tolist() == [-32767, -32767, -16383, 0, 16383, 32767, 32767]
