@@ -556,6 +556,16 @@ def run_ours_cfg2(args, rank, world, local):
     return line
 
 
+def _conv_traffic(top, b):
+    """DRAM bytes a launch of this conv shape moved in the committed ncu capture (profiles/traffic.json), or None."""
+    tp = os.path.join(REPO, "profiles", "traffic.json")
+    if not os.path.exists(tp):
+        return None
+    key = f"cin{top['Cin']}_n{top['N']}_k{top['taps']}_t{top['T']}_rows{b}"
+    e = json.load(open(tp)).get("k_conv", {}).get(key)
+    return int(e["bytes_per_unit"]) if e else None
+
+
 def conv_roofline(eng, L, dev, b, args):
     """Each decoder conv of the codec step timed alone (CUDA events around each launch on its stream, L2 flushed
     between launches); the roofline line is the conv with the largest total time (tensor-bound: its algorithmic
@@ -591,7 +601,7 @@ def conv_roofline(eng, L, dev, b, args):
     roof = {"kernel": f"k_conv (decoder op {top['op']}: Cin {top['Cin']}, N {top['N']}, taps {top['taps']}, "
                       f"T {top['T']}, {b} rows)", "bound": "tensor", "achieved": round(achieved, 1), "peak": tf,
             "unit": "TFLOP/s", "frac": round(achieved / tf, 4), "peak_kind": f"{kind} (burst bf16)",
-            "traffic": None, "algorithmic_flops_per_launch": flops[top["op"]], "us_per_launch": top["us"],
+            "traffic": _conv_traffic(top, b), "algorithmic_flops_per_launch": flops[top["op"]], "us_per_launch": top["us"],
             "all_convs": {"us_total": round(total_us, 1), "tflops": round(sum(flops) / (total_us * 1e-6) / 1e12, 1)}}
     return roof, res
 
@@ -775,7 +785,7 @@ def main():
     ap.add_argument("--admit-every", type=int, default=2, help="admit every N ticks (serve/engine_worker.py default 2)")
     ap.add_argument("--admit-batch", type=int, default=8, help="or as soon as N wait (reference default 8)")
     ap.add_argument("--max-admit", type=int, default=64)
-    ap.add_argument("--cpu-steps", type=int, default=None, help="CPU baseline sample: steps (cfg1 3, cfg2 2)")
+    ap.add_argument("--cpu-steps", type=int, default=None, help="CPU baseline sample: steps (cfg1 3, cfg2 6)")
     ap.add_argument("--cpu-rows", type=int, default=64, help="cfg2 CPU baseline sample: rows of the 192")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile", default=None, metavar="tick|conv:I|gemm",
@@ -790,7 +800,7 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     args.gpus = world if world > 1 else args.gpus
     if args.cpu_steps is None:
-        args.cpu_steps = 3 if args.workload == "cfg1" else 2
+        args.cpu_steps = 3 if args.workload == "cfg1" else 6        # ~10 s of CPU work either way
     if args.impl == "reference":
         if rank == 0:
             run_reference(args)
