@@ -102,6 +102,13 @@ class A8Engine(C.Structure):
                 ("scratch", A8Scratch), ("voc", C.POINTER(A8Vocoder)), ("side", c_void_p)]
 
 
+class A8Resample(C.Structure):
+    _fields_ = [("table", c_void_p), ("hist", c_void_p), ("n_in", c_void_p), ("n_out", c_void_p), ("left", c_void_p),
+                ("flags", c_void_p), ("up", c_int), ("down", c_int), ("taps", c_int), ("hist_len", c_int),
+                ("zpad", c_int), ("frame", c_int), ("rows", c_int), ("out_max", c_int), ("period", c_int),
+                ("half", c_ll)]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "a8_device_ok": (c_int, []),
@@ -136,6 +143,9 @@ SIGNATURES = {
     "a8_voc_step": (c_int, [C.POINTER(A8Vocoder), c_void_p, c_int, c_void_p]),
     "a8_voc_decode": (c_int, [C.POINTER(A8Vocoder), c_void_p, c_int, c_void_p]),
     "a8_state_rows": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "a8_resample_reset": (c_int, [C.POINTER(A8Resample), c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "a8_resample_step": (c_int, [C.POINTER(A8Resample), c_void_p, c_int, c_void_p, c_ll, c_int, c_void_p, c_void_p,
+                                 c_int, c_void_p, c_void_p]),
     "a8_stack_forward": (c_int, [C.POINTER(A8StackDesc), C.POINTER(A8StackRun), c_void_p]),
     "a8_tick": (c_int, [C.POINTER(A8Engine), c_int, c_void_p]),
     "a8_slow_step": (c_int, [C.POINTER(A8Engine), c_int, c_void_p]),

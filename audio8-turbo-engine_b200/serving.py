@@ -106,7 +106,8 @@ class ContinuousBatcher:
     admit(slots, reqs) -> prompt lengths (-1: rejected) and replay(b)."""
 
     def __init__(self, engine, admit_every: int = 2, admit_batch: int = 8, max_admit: int = 64, nbuf: int = 4,
-                 copy_audio: bool = True, first_chunk: int = 1, chunk_frames: int = 6):
+                 copy_audio: bool = True, first_chunk: int = 1, chunk_frames: int = 6, out_sr: Optional[int] = None,
+                 resampler=None):
         self.fe = engine
         # streamed chunks (engine_worker.py:696-697, :1246-1248): the first after `first_chunk` frames (the
         # reference's TTS_FIRST_CHUNK_FRAMES), then doubling up to `chunk_frames` (TTS_FRAMES_PER_CHUNK); the rest
@@ -120,9 +121,20 @@ class ContinuousBatcher:
         B = engine.B
         self.tok_h = pin(torch.empty(self.nbuf, B, dtype=torch.int64))
         self.aud_h = pin(torch.empty(self.nbuf, B, engine.up, dtype=torch.float32)) if copy_audio else None
+        # out_sr: each slot's audio converted to out_sr and PCM16 on the device, one launch a tick after the replay
+        # (the worker's per-request soxr stream + _pcm16, engine_worker.py:443-461); the host reads int16 rows
+        if resampler is None and out_sr is not None and int(out_sr) > 0:
+            from .resample import Resampler
+            resampler = Resampler(B, engine.sr, int(out_sr), engine.up, engine.audio.device)
+        self.rs = resampler
+        if self.rs is not None:
+            self.pcm_h = pin(torch.empty(self.nbuf, B, self.rs.out_max, dtype=torch.int16))
+            self.cnt_h = pin(torch.empty(self.nbuf, B, dtype=torch.int32))
         self.events = [torch.cuda.Event() if cuda else _HostEvent() for _ in range(self.nbuf)]
+        # on_audio(request, frame): fp32 [up] at the native rate (copy_audio), or with a resampler its int16 samples
         self.on_audio: Optional[Callable[[Request, torch.Tensor], None]] = None
-        # on_chunk(request, pcm fp32 [n * up] as numpy, final): a chunk of consecutive frames, as the worker emits
+        # on_chunk(request, pcm as numpy, final): a chunk of consecutive frames, as the worker emits -- fp32 [n * up]
+        # at the native rate, or with a resampler int16 at out_sr (the last chunk carries the flushed tail)
         self.on_chunk: Optional[Callable[[Request, np.ndarray, bool], None]] = None
 
     def run(self, requests: List[Request], follow: Optional[Callable[[Request, float], Optional[Request]]] = None,
@@ -165,6 +177,9 @@ class ContinuousBatcher:
                     else:
                         r.slot, r.t_admit = s, ta
                         rows[s] = r
+                if self.rs is not None:
+                    ok = [r for r in reqs if not r.rejected]
+                    self.rs.reset([r.slot for r in ok], [r.cap for r in ok])
                 last_admit = tick
             busy = sorted(rows)
             if busy:
@@ -174,6 +189,10 @@ class ContinuousBatcher:
                 self.tok_h[j, :b].copy_(fe.tok_in[:b], non_blocking=True)
                 if self.copy_audio:
                     self.aud_h[j, :b].copy_(fe.audio[:b], non_blocking=True)
+                if self.rs is not None:
+                    pcm, cnt = self.rs.step(fe.audio, fe.tok_in, eos, b)
+                    self.pcm_h[j, :b].copy_(pcm, non_blocking=True)
+                    self.cnt_h[j, :b].copy_(cnt, non_blocking=True)
                 self.events[j].record()
                 inflight.append((j, [(s, rows[s]) for s in busy]))
                 tick += 1
@@ -188,6 +207,7 @@ class ContinuousBatcher:
                     st.busy_time += len(snap) * (t - t_prev)
                 t_prev = t
                 toks = self.tok_h[j].tolist()
+                cnts = self.cnt_h[j].tolist() if self.rs is not None else None
                 for s, r in snap:
                     if rows.get(s) is not r:
                         continue
@@ -195,10 +215,11 @@ class ContinuousBatcher:
                         r.frames += 1
                         if r.frames == 1:
                             r.t_first = t
+                        out = self.aud_h[j, s] if self.rs is None else self.pcm_h[j, s, :cnts[s]]
                         if self.on_audio is not None:
-                            self.on_audio(r, self.aud_h[j, s])
+                            self.on_audio(r, out)
                         if self.on_chunk is not None:
-                            r.pend.append(self.aud_h[j, s].numpy().copy())
+                            r.pend.append(out.numpy().copy())
                     else:
                         r.started = True                      # the first tick decodes the silence frame
                         r.target = self.first_chunk
@@ -208,7 +229,7 @@ class ContinuousBatcher:
                         r.pend, r.chunks = [], r.chunks + 1
                         r.target = min(self.chunk_frames, r.target * 2)
                     elif self.on_chunk is not None and end:
-                        self.on_chunk(r, np.zeros(0, np.float32), True)
+                        self.on_chunk(r, np.zeros(0, np.float32 if self.rs is None else np.int16), True)
                     if end:
                         r.eos = toks[s] == eos
                         r.t_done = t

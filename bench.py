@@ -621,7 +621,9 @@ def serve_dict(args, world):
              + (f", assigned to {world} replicas by least-loaded slot count" if world > 1 else ""))
     return {"workload": w + "; prompts U[20,200] random ids, one of 8 cached voices (150-frame prefixes), output "
                             "geometric mean 300 frames capped 1024; ragged packed prefill into running ticks, "
-                            f"max_slots {args.slots}",
+                            f"max_slots {args.slots}; audio out "
+                            + (f"int16 at {args.out_sr} Hz (GPU resampler + PCM16)" if args.out_sr
+                               else "fp32 at 44.1 kHz"),
             "model": "Audio8 stand-in (seeded random weights, reference shapes)", "parallelism": f"replicas x{world}",
             "timing": "wall clock, as the reference's serving numbers (RTF = wall time / audio length, TTFA "
                       "included); the first tick of a row (its silence frame) is not audio"}
@@ -663,7 +665,7 @@ def run_serving(args, rank, world, local):
     warm = [S.Request(rid=-1 - i, arrival=0.0, text=" ".join(["7"] * 20), item=voices[i % len(voices)][1],
                       key=voices[i % len(voices)][0], cap=4) for i in range(min(64, args.slots))]
     bat = S.ContinuousBatcher(eng, admit_every=args.admit_every, admit_batch=args.admit_batch,
-                              max_admit=args.max_admit)
+                              max_admit=args.max_admit, copy_audio=not args.out_sr, out_sr=args.out_sr or None)
     bat.run(warm)
     torch.cuda.synchronize()
     eng.reset_state()
@@ -704,8 +706,11 @@ def run_serving(args, rank, world, local):
             "frames_per_s": round(frames / wall, 1), "finished": int(len(rtf)),
             "per_rank": [a["summary"] for a in allr], "build_s": round(t_build, 1), "clocks": clk.summary(),
             "e2e": {"value": round(value, 1), "unit": "streams", "h2d_bytes_per_step": None,
-                    "d2h_bytes_per_step": eng.B * (8 + 4 * eng.up), "note": "the trace is end to end by itself: "
-                    "prompts in, every tick's tokens and audio read back to pinned host memory"}}
+                    "d2h_bytes_per_step": eng.B * (8 + (4 + 2 * bat.rs.out_max if bat.rs is not None
+                                                        else 4 * eng.up)),
+                    "note": "the trace is end to end by itself: prompts in, every tick's tokens and audio read back "
+                            "to pinned host memory" + (f" (int16 at {args.out_sr} Hz, converted on the GPU)"
+                                                       if args.out_sr else " (fp32 at the codec rate)")}}
     return line
 
 
@@ -748,9 +753,11 @@ def run_profile(args):
     import ctypes as C
 
     import torch
+    what = args.profile
+    if what == "resample":
+        return profile_resample()
     a8, eng, step = cfg2_engine()
     L = a8._lib
-    what = args.profile
     if what == "tick":
         fn = step
     elif what.startswith("conv:"):
@@ -758,7 +765,7 @@ def run_profile(args):
         run = eng.voc.conv_run(i, B_CFG2)
         fn = lambda: L.call("a8_conv", C.byref(run), L.stream_handle())
     else:
-        raise SystemExit(f"--profile {what}: expected tick or conv:I")
+        raise SystemExit(f"--profile {what}: expected tick, conv:I or resample")
     for _ in range(2):
         step()
     torch.cuda.synchronize()
@@ -769,6 +776,47 @@ def run_profile(args):
     err = a8.device_error()
     assert err[0] == 0, err
     print(json.dumps({"profile": what, "ok": True}), flush=True)
+
+
+def profile_resample(b=B_CFG2, ticks=20):
+    """The per-slot resampler (44.1 -> 16 kHz + PCM16) at the cfg2 bucket: `ticks` timed steps (CUDA events), then
+    one step inside cudaProfilerStart/Stop. Prints one JSON line with the step time and its FMA rate."""
+    import importlib
+
+    import torch
+
+    import __graft_entry__ as G
+    G.build()
+    a8 = G.load_package()
+    RS = importlib.import_module(a8.__name__ + ".resample")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    rs = RS.Resampler(b, 44100, 16000, 2048, dev)
+    g = torch.Generator(device=dev).manual_seed(5)
+    audio = (torch.rand(b, 2048, generator=g, device=dev) - 0.5).float()
+    tok = torch.zeros(b, dtype=torch.int64, device=dev)
+    rs.reset(list(range(b)), [1 << 30] * b, drop_first=False)
+    for _ in range(3):
+        rs.step(audio, tok, -1, b)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    outs = 0
+    e0.record()
+    for _ in range(ticks):
+        _, cnt = rs.step(audio, tok, -1, b)
+    e1.record()
+    torch.cuda.synchronize()
+    outs = int(cnt.sum())
+    us = e0.elapsed_time(e1) * 1000 / ticks
+    torch.cuda.profiler.start()
+    rs.step(audio, tok, -1, b)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    err = a8.device_error()
+    assert err[0] == 0, err
+    fma = outs * rs.taps
+    print(json.dumps({"profile": "resample", "ok": True, "rows": b, "us_per_step": round(us, 2),
+                      "outputs_per_step": outs, "taps": rs.taps, "gfma_per_s": round(fma / us / 1e3, 1),
+                      "bytes_per_step": b * (2048 * 4 + rs.out_max * 2 + 2 * rs.hist_len * 4)}), flush=True)
 
 
 def main():
@@ -788,9 +836,13 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=None, help="CPU baseline sample: steps (cfg1 3, cfg2 6)")
     ap.add_argument("--cpu-rows", type=int, default=64, help="cfg2 CPU baseline sample: rows of the 192")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--profile", default=None, metavar="tick|conv:I|gemm",
-                    help="no timing: run one eager cfg2 tick (or decoder conv I alone at 192 rows) between "
-                         "cudaProfilerStart/Stop, for ncu --profile-from-start off")
+    ap.add_argument("--profile", default=None, metavar="tick|conv:I|resample",
+                    help="no timing: run one eager cfg2 tick (or decoder conv I alone at 192 rows, or the 44.1 -> "
+                         "16 kHz resampler step at 192 rows) between cudaProfilerStart/Stop, for ncu "
+                         "--profile-from-start off")
+    ap.add_argument("--out-sr", type=int, default=16000,
+                    help="cfg3/streams: each stream converted to this rate + PCM16 on the GPU (the worker's "
+                         "TTS_OUT_SR; 0 = read back fp32 frames at the codec rate)")
     args = ap.parse_args()
     if args.profile:
         return run_profile(args)

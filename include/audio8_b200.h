@@ -329,6 +329,37 @@ enum { A8_STATE_CLEAR = 0, A8_STATE_LOAD = 1, A8_STATE_SNAPSHOT = 2 };
 int a8_state_rows(const A8StateSeg* segs, int nseg, const int* slots, int nslots, int op, void* blob,
                   a8_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------- resampler */
+/* Per-slot streaming rate conversion of the codec's audio (native rate -> out rate, e.g. 44.1 -> 16 kHz) and PCM16,
+ * replacing the worker's post-processing per request (serve/engine_worker.py:443-449 soxr.ResampleStream(native_sr,
+ * out_sr, 1, dtype="float32"), :460-461 resample_chunk(y, last=final), :423-424 _pcm16). A linear-phase FIR h of
+ * odd length L = 2 half + 1 at the up-sampled rate: output n = sum_k table[k][p] x[m - k] with q = n down + half,
+ * m = q / up, p = q % up and x beyond the input zero; the output is delay-compensated (output 0 is centred on input
+ * 0) and a stream of N inputs yields ceil(N up / down) outputs in all. */
+typedef struct A8Resample {
+  const float* table;     /* [taps, up]: table[k][p] = up * h[p + k up] (0 past L) */
+  float* hist;            /* [rows, hist_len] the last hist_len input samples of each slot */
+  long long* n_in;        /* [rows] input samples taken so far */
+  long long* n_out;       /* [rows] output samples given so far */
+  int* left;              /* [rows] frames the slot still takes (its frame cap) */
+  int* flags;             /* [rows] bit 0: drop the next frame (the silence frame); bit 1: stream ended */
+  int up, down, taps, hist_len, zpad, frame, rows, out_max, period;
+  long long half;
+} A8Resample;
+
+/* Start a stream in each of slots[0, n) (int32, device): history zeroed, counters 0, `caps[i]` (int32, device)
+ * frames, the first frame dropped when drop_first (the frame a fresh slot decodes from the silence frame). */
+int a8_resample_reset(const A8Resample* d, const int* slots, const int* caps, int n, int drop_first,
+                      a8_stream_t stream);
+
+/* One frame for slot rows [0, b): audio fp32 [b, ld_audio] (frame samples a row), tok_in int64 [b] = the token each
+ * row consumed this tick. A live row takes its frame; when it consumed `eos` or used its last capped frame the frame
+ * is its last and the stream is flushed (zeros past the end). counts[r] = outputs written this step: pcm int16
+ * [b, ld_out] (clip to [-1, 1], x 32767, truncated) and, when f32 is not NULL, the fp32 samples [b, ld_out]. Rows
+ * whose stream ended, and a dropped frame, give 0 outputs. */
+int a8_resample_step(const A8Resample* d, const float* audio, int ld_audio, const int64_t* tok_in, long long eos,
+                     int b, int16_t* pcm, float* f32, int ld_out, int* counts, a8_stream_t stream);
+
 /* ---------------------------------------------------------------------------------------------- engine */
 typedef struct A8Engine {
   int B, S, H, ncb, cbk, nsem, vocab, ras_w;

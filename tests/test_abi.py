@@ -40,7 +40,7 @@ def test_struct_layouts_match_header(a8):
     for cname, cls in (("A8Epilogue", L.A8Epilogue), ("A8Scratch", L.A8Scratch), ("A8StackDesc", L.A8StackDesc),
                        ("A8StackRun", L.A8StackRun), ("A8Engine", L.A8Engine), ("A8ConvOp", L.A8ConvOp),
                        ("A8Upsample", L.A8Upsample), ("A8Vocoder", L.A8Vocoder), ("A8StateSeg", L.A8StateSeg),
-                       ("A8ConvRun", L.A8ConvRun), ("A8CtxShift", L.A8CtxShift)):
+                       ("A8ConvRun", L.A8ConvRun), ("A8CtxShift", L.A8CtxShift), ("A8Resample", L.A8Resample)):
         body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), src, flags=re.S).group(1)
         fields = []
         for decl in body.split(";"):

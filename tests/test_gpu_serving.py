@@ -4,6 +4,7 @@ the covering bucket, deliver one frame of audio a tick after their silence frame
 reused. Checks the delivered audio against the engine's own audio rows and the bookkeeping of every request."""
 import importlib
 
+import numpy as np
 import pytest
 import torch
 
@@ -48,3 +49,30 @@ def test_serving_loop_on_engine(a8, serving, tiny_model):
     # more requests than slots: slots were reused, and at most 6 rows were ever busy
     assert max(st.buckets) <= 6 and len({r.slot for r in reqs}) <= 6
     assert sum(r.frames for r in reqs) == s["frames"]
+
+
+def test_serving_loop_resampled(a8, serving, tiny_model):
+    """out_sr=16000: every request's chunks are int16 at 16 kHz, ceil(frames x 2048 x 160 / 441) samples in all (its
+    stream flushed on its last frame), and the first chunk is ready after one frame."""
+    gp = dict(do_sample=True, temperature=0.8, top_k=50, top_p=0.95, max_new_tokens=64)
+    eng = a8.FastEngine(tiny_model, StubTokenizer(), gp, max_slots=6, max_seq=512, buckets=[2, 4, 6],
+                        seq_from_env=False, seed=6)
+    eng.capture(log=lambda *a: None)
+    ncb = int(tiny_model.config.num_codebooks)
+    voices = serving.voice_items(2, 12, ncb, seed=4)
+    serving.warm_voices(eng, voices)
+    caps = [5, 9, 3, 12, 7, 4, 6, 8]
+    reqs = [serving.Request(rid=i, arrival=0.01 * i, text=" ".join(str(200 + i + k) for k in range(8 + i)),
+                            item=voices[i % 2][1], key=voices[i % 2][0], cap=c) for i, c in enumerate(caps)]
+    loop = serving.ContinuousBatcher(eng, admit_every=1, admit_batch=4, copy_audio=False, out_sr=16000)
+    got = {}
+    loop.on_chunk = lambda r, y, final: got.setdefault(r.rid, []).append((y.copy(), final))
+    loop.run(reqs)
+    assert a8.device_error()[0] == 0
+    for r in reqs:
+        chunks = got[r.rid]
+        assert all(y.dtype == np.int16 for y, _ in chunks) and [f for _, f in chunks][-1]
+        n = sum(len(y) for y, _ in chunks)
+        assert n == -(-r.frames * eng.up * 160 // 441), (r.rid, r.frames, n)
+        if r.frames:
+            assert len(chunks[0][0]) <= 743 + 90 and np.abs(np.concatenate([y for y, _ in chunks])).max() > 0

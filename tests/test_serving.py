@@ -250,3 +250,59 @@ def test_pcm16(serving):
     y = np.array([-2.0, -1.0, -0.5, 0.0, 0.5, 1.0, 3.0], dtype=np.float32)
     out = np.frombuffer(serving.pcm16(y), dtype="<i2")
     assert out.tolist() == [-32767, -32767, -16383, 0, 16383, 32767, 32767]
+
+
+class FakeResampler:
+    """The device resampler's per-slot contract on the CPU: the first frame of a stream dropped, 2 samples a frame
+    (value = the frame's audio), 3 more (-1) when the frame is the stream's last (EOS consumed or cap reached)."""
+
+    out_max = 8
+
+    def __init__(self, B):
+        self.skip, self.left, self.done = [False] * B, [0] * B, [True] * B
+        self.pcm = torch.zeros(B, self.out_max, dtype=torch.int16)
+        self.cnt = torch.zeros(B, dtype=torch.int32)
+        self.resets = []
+
+    def reset(self, slots, caps):
+        self.resets.append(list(slots))
+        for s, c in zip(slots, caps):
+            self.skip[s], self.left[s], self.done[s] = True, c, False
+
+    def step(self, audio, tok_in, eos, b):
+        self.cnt.zero_()
+        for r in range(b):
+            end = int(tok_in[r]) == eos
+            if self.done[r]:
+                continue
+            if self.skip[r]:
+                self.skip[r], self.done[r] = False, end
+                continue
+            self.left[r] -= 1
+            last = end or self.left[r] <= 0
+            n = 5 if last else 2
+            self.pcm[r, :2] = int(audio[r, 0])
+            self.pcm[r, 2:5] = -1
+            self.cnt[r] = n
+            self.done[r] = last
+        return self.pcm[:b], self.cnt[:b]
+
+
+def test_resampled_chunks(serving):
+    """With a resampler the loop resets a slot's stream on admission, steps it every tick and delivers int16 chunks
+    whose samples are exactly the resampler's rows: the silence frame gives none, the last frame carries the tail."""
+    fe = FakeEngine()
+    rs = FakeResampler(fe.B)
+    got = {}
+    b = serving.ContinuousBatcher(fe, resampler=rs, copy_audio=False, first_chunk=1, chunk_frames=2)
+    b.on_chunk = lambda r, y, final: got.setdefault(r.rid, []).append((y.dtype, y.tolist(), final))
+    clk = FakeClock()
+    reqs = [_req(serving, 0, 0.0, cap=4), _req(serving, 1, 0.0, cap=9, eos_at=3), _req(serving, 2, 0.0, cap=5, eos_at=1)]
+    b.run(reqs, clock=clk, sleep=clk.sleep)
+    assert rs.resets == [[0, 1, 2]]
+    assert all(d == np.int16 for c in got.values() for d, _, _ in c)
+    flat = lambda rid: [v for _, vs, _ in got[rid] for v in vs]
+    assert flat(0) == [2, 2, 3, 3, 4, 4, 5, 5, -1, -1, -1]            # ticks 2-5, the tail on the capped frame
+    assert [f for _, _, f in got[0]] == [False, False, True]           # chunks of 1, 2, then the rest
+    assert flat(1) == [2, 2, 3, 3, -1, -1, -1]                         # EOS consumed on tick 3
+    assert got[2] == [(np.int16, [], True)]                            # EOS on the silence tick: an empty final chunk
