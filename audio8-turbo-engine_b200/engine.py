@@ -22,6 +22,7 @@ import numpy as np
 import torch
 
 from . import _lib as L
+from .snapstore import SnapStore, ref_fp
 
 BF16 = torch.bfloat16
 
@@ -187,7 +188,7 @@ class FastEngine:
         # of its voice's reference decoded (prime_speakers)
         self.voc_prime = os.environ.get("TTS_VOC_PRIME", "0").strip().lower() not in ("0", "false", "no", "off")
         self.prime_frames = max(2, int(os.environ.get("TTS_VOC_PRIME_FRAMES", "160")))
-        self.voc_snaps: Dict[str, tuple] = {}
+        self.voc_snaps = SnapStore()                # memory only; a worker may install one with a disk cache
         self.side = torch.cuda.Stream(device=dev)
 
         # persistent per-slot state (fixed addresses; row B = SCR, prefill padding)
@@ -413,6 +414,8 @@ class FastEngine:
             return
         todo, seen = [], set()
         for key, item in pairs:
+            if getattr(self.voc_snaps, "path", None):   # its file is named by the codes it is made from
+                self.voc_snaps.set_fp(key, ref_fp(item))
             if key not in self.voc_snaps and key not in seen:
                 seen.add(key)
                 todo.append((key, item))

@@ -137,3 +137,36 @@ def test_voice_priming(a8, dev, tiny_model, monkeypatch):
         s = snr_db(audio[r], w[0])
         print(f"row {r}: first audio frame after {len(frames) - 1} primed frames, SNR {s:.1f} dB")
         assert s >= 38.0, (r, s)
+
+
+def test_voice_snapshots_on_disk(a8, dev, tiny_model, monkeypatch, tmp_path):
+    """A disk-backed store (the worker's TTS_SNAP_DIR): priming writes one file a voice; a second engine on the same
+    directory primes nothing, reads the snapshot back on the voice's first admission, and starts the row from it."""
+    from types import SimpleNamespace
+    from audio8_b200.snapstore import SnapStore
+    monkeypatch.setenv("TTS_VOC_PRIME", "1")
+    monkeypatch.setenv("TTS_VOC_PRIME_FRAMES", "4")
+    gp = dict(do_sample=True, temperature=0.8, top_k=50, top_p=0.95, max_new_tokens=64)
+    g = torch.Generator().manual_seed(23)
+    items = [(f"v{k}", SimpleNamespace(ref_code=torch.randint(0, 4096, (9, 10), generator=g), ref_text="12 34"))
+             for k in range(2)]
+    engs = []
+    for _ in range(2):
+        eng = a8.FastEngine(tiny_model, StubTokenizer(), gp, max_slots=2, max_seq=512, buckets=[2],
+                            seq_from_env=False, seed=43)
+        eng.voc_snaps = SnapStore(str(tmp_path), ram=1)
+        eng.prime_speakers(items)
+        torch.cuda.synchronize()
+        engs.append(eng)
+    first, second = engs
+    assert first.voc_snaps.on_disk() == 2 and second.voc_snaps.loads == 0 and len(second.voc_snaps) == 0
+    reqs = [dict(text="10 11 12 13", item=items[1][1], key="v1"), dict(text="14 15", item=items[0][1], key="v0")]
+    second.admit([0, 1], reqs)
+    torch.cuda.synchronize()
+    assert a8.device_error()[0] == 0 and second.voc_snaps.loads == 2
+    assert torch.equal(_blob(second, 0), _blob_of(first, "v1")) and torch.equal(_blob(second, 1), _blob_of(first, "v0"))
+    assert torch.equal(second.frame_prev[0].cpu(), items[1][1].ref_code[-1])
+
+
+def _blob_of(eng, key):
+    return eng.voc_snaps[key][0][0].reshape(1, -1).cpu()
