@@ -21,7 +21,6 @@ tests/test_oracle_golden.py checks this module against them.
 """
 from __future__ import annotations
 
-import math
 from types import SimpleNamespace
 from typing import Dict, List, Optional, Sequence
 
