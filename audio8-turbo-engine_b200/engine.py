@@ -369,6 +369,8 @@ class FastEngine:
 
     @torch.inference_mode()
     def build_prompts(self, reqs):
+        if not reqs:
+            return []
         if self._parts is None:
             self._parts_init()
         P = self._parts
@@ -476,6 +478,8 @@ class FastEngine:
     @torch.inference_mode()
     def admit(self, slots: List[int], reqs: List[dict]):
         """Packed prefill of reqs into free slots. Returns each prompt's length, or -1 for one that can't fit."""
+        if not reqs:
+            return []
         parts = self.build_prompts(reqs)
         lens = [(p.shape[0] if p is not None else 0) + r.shape[0] for _, p, r in parts]
         limit = min(self.S - 32, self.prefill_tokens)
@@ -513,15 +517,25 @@ class FastEngine:
         ns = [int(r.shape[0]) for r in rests]
         starts = [p0.get(s, 0) for s in slots]
         x = torch.cat(rests, 0).contiguous()
-        pos = torch.cat([torch.arange(a, a + n, dtype=torch.int32) for a, n in zip(starts, ns)]).to(dev)
+        pos_h = torch.cat([torch.arange(a, a + n, dtype=torch.int32) for a, n in zip(starts, ns)])
+        pos = pos_h.to(dev)
         slot_t = torch.cat([torch.full((n,), s, dtype=torch.int32) for n, s in zip(ns, slots)]).to(dev)
-        max_len = max(a + n for a, n in zip(starts, ns))
-        h = self._forward_rows(x, pos, slot_t, max_len)
-        last = torch.tensor(np.cumsum(ns) - 1, dtype=torch.int32, device=dev)
-        k = len(slots)
-        self.pf_last[:k].copy_(last)
-        L.call("a8_gather_rows", L.ptr(h), self.H, L.ptr(self.pf_last), L.ptr(self.pf_hl), self.H, k, self.H,
-               L.stream_handle())
+        ends = np.cumsum(ns) - 1
+        k, T = len(slots), x.shape[0]
+        # the packed rows in pieces of at most pf_rows: a request may span pieces (its later rows attend to the keys
+        # its earlier rows stored); each request's last row is gathered from the piece it ends in
+        i0 = 0
+        for a in range(0, T, self.pf_rows):
+            e = min(T, a + self.pf_rows)
+            h = self._forward_rows(x[a:e], pos[a:e], slot_t[a:e], int(pos_h[a:e].max()) + 1)
+            i1 = i0
+            while i1 < k and ends[i1] < e:
+                i1 += 1
+            if i1 > i0:
+                self.pf_last[i0:i1].copy_(torch.tensor(ends[i0:i1] - a, dtype=torch.int32))
+                L.call("a8_gather_rows", L.ptr(h), self.H, L.ptr(self.pf_last[i0:]), L.ptr(self.pf_hl[i0]), self.H,
+                       i1 - i0, self.H, L.stream_handle())
+            i0 = i1
         self.pf_st[:k].copy_(torch.tensor(slots, dtype=torch.int32))
         self.pf_cpos[:k].copy_(torch.tensor([a + n for a, n in zip(starts, ns)], dtype=torch.int32))
         L.call("a8_prefill_finish", C.byref(self.desc), L.ptr(self.pf_hl), k, L.ptr(self.pf_st), L.ptr(self.pf_cpos),
