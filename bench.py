@@ -56,17 +56,21 @@ class Clocks:
          "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index):
-        self.index, self.rows, self.proc = index, [], None
+        self.index, self.rows, self.proc, self.n0 = index, [], None, 0
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                          "--format=csv,noheader,nounits", "-lms", "50"], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()                     # the timed region starts once samples are flowing (<= 3 s)
+            while not self.rows and time.time() - t0 < 3.0 and self.proc.poll() is None:
+                time.sleep(0.01)
         except (OSError, FileNotFoundError):
             self.proc = None
+        self.n0 = len(self.rows)                 # samples taken before the region are not counted (if others came)
         return self
 
     def _read(self):
@@ -83,7 +87,7 @@ class Clocks:
             self.t.join(timeout=2)
 
     def summary(self):
-        rows = [r for r in self.rows if len(r) >= 9]
+        rows = [r for r in self.rows[self.n0:] if len(r) >= 9] or [r for r in self.rows if len(r) >= 9]
         if not rows:
             return None
         sm = sorted(float(r[1]) for r in rows)
