@@ -72,7 +72,7 @@ def test_struct_sizes_match_c_compiler(a8, tmp_path):
     structs = {"A8Epilogue": L.A8Epilogue, "A8Scratch": L.A8Scratch, "A8StackDesc": L.A8StackDesc,
                "A8StackRun": L.A8StackRun, "A8Engine": L.A8Engine, "A8ConvOp": L.A8ConvOp,
                "A8Upsample": L.A8Upsample, "A8Vocoder": L.A8Vocoder, "A8StateSeg": L.A8StateSeg,
-               "A8ConvRun": L.A8ConvRun, "A8CtxShift": L.A8CtxShift}
+               "A8ConvRun": L.A8ConvRun, "A8CtxShift": L.A8CtxShift, "A8Resample": L.A8Resample}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "audio8_b200.h"', 'int main(void) {']
     for cname, cls in structs.items():
         lines.append(f'printf("{cname} sizeof %zu\\n", sizeof({cname}));')
