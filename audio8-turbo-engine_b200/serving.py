@@ -49,6 +49,7 @@ class Request:
     t_done: Optional[float] = None
     eos: bool = False
     rejected: bool = False
+    cancelled: bool = False       # the client went away (engine_worker.py:1125-1143): ended without its audio
     pend: list = field(default_factory=list)   # frames not yet emitted as a chunk
     target: int = 0                            # frames the next chunk waits for
     chunks: int = 0
@@ -69,7 +70,7 @@ class RunStats:
     buckets: Dict[int, int] = field(default_factory=dict)
 
     def finished(self):
-        return [r for r in self.requests if r.t_done is not None and r.frames > 0]
+        return [r for r in self.requests if r.t_done is not None and r.frames > 0 and not r.cancelled]
 
     def summary(self):
         done = self.finished()
@@ -80,6 +81,7 @@ class RunStats:
         return {
             "requests": len(self.requests), "finished": len(done),
             "rejected": sum(r.rejected for r in self.requests), "eos": sum(r.eos for r in done),
+            "cancelled": sum(r.cancelled for r in self.requests),
             "ttfa_ms_p50": round(pct(ttfa, 50), 1), "ttfa_ms_p95": round(pct(ttfa, 95), 1),
             "rtf_p50": round(pct(rtf, 50), 4), "rtf_p95": round(pct(rtf, 95), 4),
             "mean_streams": round(self.busy_time / max(1e-9, self.wall), 1),
@@ -136,6 +138,13 @@ class ContinuousBatcher:
         # on_chunk(request, pcm as numpy, final): a chunk of consecutive frames, as the worker emits -- fp32 [n * up]
         # at the native rate, or with a resampler int16 at out_sr (the last chunk carries the flushed tail)
         self.on_chunk: Optional[Callable[[Request, np.ndarray, bool], None]] = None
+        self._cancels: deque = deque()
+
+    def cancel(self, rid: int):
+        """The client of request `rid` went away (the worker's ("__cancel__", rid) message): a running request ends
+        at the next iteration and frees its slot, a waiting one is dropped; either gets an empty final chunk (the
+        worker's end-of-stream). Safe to call from callbacks or another thread; unknown or ended ids are ignored."""
+        self._cancels.append(rid)
 
     def run(self, requests: List[Request], follow: Optional[Callable[[Request, float], Optional[Request]]] = None,
             clock=time.perf_counter, sleep=time.sleep) -> RunStats:
@@ -154,12 +163,32 @@ class ContinuousBatcher:
         t0 = clock()
         now = lambda: clock() - t0
         t_prev = None
+        def end_cancelled(r, t):
+            r.cancelled, r.t_done, r.pend = True, t, []
+            if self.on_chunk is not None:
+                self.on_chunk(r, np.zeros(0, np.float32 if self.rs is None else np.int16), True)
+
         while pending or waiting or rows or inflight:
             t = now()
+            while self._cancels:
+                rid = self._cancels.popleft()
+                s_run = next((s for s, r in rows.items() if r.rid == rid), None)
+                if s_run is not None:
+                    r = rows.pop(s_run)
+                    heapq.heappush(free, s_run)
+                    end_cancelled(r, t)
+                    continue
+                for q in (waiting, pending):
+                    r = next((r for r in q if r.rid == rid), None)
+                    if r is not None:
+                        q.remove(r)
+                        end_cancelled(r, t)
+                        break
             while pending and pending[0].arrival <= t:
                 waiting.append(pending.popleft())
             if not rows and not waiting and not inflight:
-                sleep(max(0.0, min(0.05, pending[0].arrival - t)))   # idle until the next arrival
+                if pending:                                   # idle until the next arrival (none left: done)
+                    sleep(max(0.0, min(0.05, pending[0].arrival - t)))
                 t_prev = None
                 continue
             if waiting and free and (not rows or tick - last_admit >= self.admit_every

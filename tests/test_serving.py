@@ -306,3 +306,44 @@ def test_resampled_chunks(serving):
     assert [f for _, _, f in got[0]] == [False, False, True]           # chunks of 1, 2, then the rest
     assert flat(1) == [2, 2, 3, 3, -1, -1, -1]                         # EOS consumed on tick 3
     assert got[2] == [(np.int16, [], True)]                            # EOS on the silence tick: an empty final chunk
+
+
+def test_cancel_running_and_waiting(serving):
+    """A client that goes away (the worker's ("__cancel__", rid)): a running request ends with an empty final chunk and
+    frees its slot for the next request; a waiting one is never admitted; ids that are unknown or already ended are
+    ignored; cancelled requests are counted apart from the finished ones."""
+    fe = FakeEngine(B=1, buckets=(1,))
+    reqs = [_req(serving, 0, 0.0, cap=50), _req(serving, 1, 0.0, cap=3), _req(serving, 2, 0.0, cap=4)]
+    loop = serving.ContinuousBatcher(fe, admit_every=1)
+    got = {}
+
+    def on_chunk(r, y, final):
+        got.setdefault(r.rid, []).append((len(y), final))
+        if r.rid == 0 and r.frames >= 5 and not got.get("sent"):
+            got["sent"] = True
+            loop.cancel(0)          # running: ends at the next iteration
+            loop.cancel(2)          # waiting behind it: dropped
+            loop.cancel(99)         # unknown: ignored
+    loop.on_chunk = on_chunk
+    clk = FakeClock()
+    st = loop.run(reqs, clock=clk, sleep=clk.sleep)
+    r0, r1, r2 = reqs
+    assert r0.cancelled and 5 <= r0.frames < 50 and got[0][-1] == (0, True)
+    assert r2.cancelled and r2.slot == -1 and r2.frames == 0 and got[2] == [(0, True)]
+    assert not r1.cancelled and r1.frames == 3 and r1.slot == 0 and r1.t_admit >= r0.t_done
+    s = st.summary()
+    assert s["cancelled"] == 2 and s["finished"] == 1
+    loop.cancel(1)                  # already ended: nothing happens on a later run
+    loop.run([], clock=clk, sleep=clk.sleep)
+    assert not r1.cancelled
+
+
+def test_cancel_last_pending_ends_run(serving):
+    """Cancelling the only request not yet arrived ends the run instead of waiting for it."""
+    fe = FakeEngine()
+    loop = serving.ContinuousBatcher(fe)
+    reqs = [_req(serving, 0, 0.0, cap=2), _req(serving, 1, 100.0, cap=2)]
+    loop.on_audio = lambda r, a: loop.cancel(1)
+    clk = FakeClock()
+    st = loop.run(reqs, clock=clk, sleep=clk.sleep)
+    assert reqs[1].cancelled and reqs[1].t_admit is None and st.wall < 100.0
