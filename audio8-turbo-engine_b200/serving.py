@@ -50,6 +50,7 @@ class Request:
     eos: bool = False
     rejected: bool = False
     cancelled: bool = False       # the client went away (engine_worker.py:1125-1143): ended without its audio
+    error: Optional[str] = None   # why it failed (engine_worker.py:828-832, :883, :893, :1186-1190)
     pend: list = field(default_factory=list)   # frames not yet emitted as a chunk
     target: int = 0                            # frames the next chunk waits for
     chunks: int = 0
@@ -70,7 +71,8 @@ class RunStats:
     buckets: Dict[int, int] = field(default_factory=dict)
 
     def finished(self):
-        return [r for r in self.requests if r.t_done is not None and r.frames > 0 and not r.cancelled]
+        return [r for r in self.requests if r.t_done is not None and r.frames > 0 and not r.cancelled
+                and r.error is None]
 
     def summary(self):
         done = self.finished()
@@ -82,6 +84,7 @@ class RunStats:
             "requests": len(self.requests), "finished": len(done),
             "rejected": sum(r.rejected for r in self.requests), "eos": sum(r.eos for r in done),
             "cancelled": sum(r.cancelled for r in self.requests),
+            "failed": sum(r.error is not None and not r.rejected for r in self.requests),
             "ttfa_ms_p50": round(pct(ttfa, 50), 1), "ttfa_ms_p95": round(pct(ttfa, 95), 1),
             "rtf_p50": round(pct(rtf, 50), 4), "rtf_p95": round(pct(rtf, 95), 4),
             "mean_streams": round(self.busy_time / max(1e-9, self.wall), 1),
@@ -138,6 +141,8 @@ class ContinuousBatcher:
         # on_chunk(request, pcm as numpy, final): a chunk of consecutive frames, as the worker emits -- fp32 [n * up]
         # at the native rate, or with a resampler int16 at out_sr (the last chunk carries the flushed tail)
         self.on_chunk: Optional[Callable[[Request, np.ndarray, bool], None]] = None
+        # on_error(request, message): the worker's ("__error__", message), followed by the request's final chunk
+        self.on_error: Optional[Callable[[Request, str], None]] = None
         self._cancels: deque = deque()
 
     def cancel(self, rid: int):
@@ -163,10 +168,21 @@ class ContinuousBatcher:
         t0 = clock()
         now = lambda: clock() - t0
         t_prev = None
-        def end_cancelled(r, t):
-            r.cancelled, r.t_done, r.pend = True, t, []
+        def end_stream(r):
             if self.on_chunk is not None:
                 self.on_chunk(r, np.zeros(0, np.float32 if self.rs is None else np.int16), True)
+
+        def end_cancelled(r, t):
+            r.cancelled, r.t_done, r.pend = True, t, []
+            end_stream(r)
+
+        def end_failed(r, msg, t):
+            r.error, r.pend = msg, []
+            if t is not None:
+                r.t_done = t
+            if self.on_error is not None:
+                self.on_error(r, msg)
+            end_stream(r)
 
         while pending or waiting or rows or inflight:
             t = now()
@@ -196,24 +212,42 @@ class ContinuousBatcher:
                 take = min(len(waiting), len(free), self.max_admit)
                 slots = [heapq.heappop(free) for _ in range(take)]
                 reqs = [waiting.popleft() for _ in range(take)]
-                lens = fe.admit(slots, [r.as_admit() for r in reqs])
+                try:
+                    lens = fe.admit(slots, [r.as_admit() for r in reqs])
+                except Exception:                             # the whole admission fails; its slots are freed
+                    lens = None
                 st.admits += 1
                 ta = now()
-                for r, s, n in zip(reqs, slots, lens):
-                    if n < 0:                                 # prompt too long for the engine
-                        r.rejected = True
+                if lens is None:
+                    for r, s in zip(reqs, slots):
                         heapq.heappush(free, s)
-                    else:
-                        r.slot, r.t_admit = s, ta
-                        rows[s] = r
-                if self.rs is not None:
-                    ok = [r for r in reqs if not r.rejected]
-                    self.rs.reset([r.slot for r in ok], [r.cap for r in ok])
+                        end_failed(r, "engine error", ta)
+                else:
+                    for r, s, n in zip(reqs, slots, lens):
+                        if n < 0:                             # prompt too long for the engine
+                            r.rejected = True
+                            heapq.heappush(free, s)
+                            end_failed(r, "text too long for TTS_MAX_SEQ", None)
+                        else:
+                            r.slot, r.t_admit = s, ta
+                            rows[s] = r
+                    if self.rs is not None:
+                        ok = [r for r in reqs if not r.rejected]
+                        self.rs.reset([r.slot for r in ok], [r.cap for r in ok])
                 last_admit = tick
             busy = sorted(rows)
             if busy:
                 b = fe.bucket_for(busy[-1] + 1)
-                fe.replay(b)
+                try:
+                    fe.replay(b)
+                except Exception:                             # a failed tick ends every running row
+                    tf = now()
+                    for s in busy:
+                        heapq.heappush(free, s)
+                        end_failed(rows.pop(s), "engine error", tf)
+                    inflight.clear()
+                    t_prev = None
+                    continue
                 j = tick % self.nbuf
                 self.tok_h[j, :b].copy_(fe.tok_in[:b], non_blocking=True)
                 if self.copy_audio:

@@ -347,3 +347,64 @@ def test_cancel_last_pending_ends_run(serving):
     clk = FakeClock()
     st = loop.run(reqs, clock=clk, sleep=clk.sleep)
     assert reqs[1].cancelled and reqs[1].t_admit is None and st.wall < 100.0
+
+
+class FlakyEngine(FakeEngine):
+    """Raises on the admissions / ticks whose (1-based) call numbers are listed."""
+
+    def __init__(self, bad_admits=(), bad_ticks=(), **kw):
+        super().__init__(**kw)
+        self.bad_admits, self.bad_ticks, self.n_admit, self.n_tick = set(bad_admits), set(bad_ticks), 0, 0
+
+    def admit(self, slots, reqs):
+        self.n_admit += 1
+        if self.n_admit in self.bad_admits:
+            raise RuntimeError("admit failed")
+        return super().admit(slots, reqs)
+
+    def replay(self, b):
+        self.n_tick += 1
+        if self.n_tick in self.bad_ticks:
+            raise RuntimeError("tick failed")
+        super().replay(b)
+
+
+def _run_flaky(serving, fe, reqs, **kw):
+    loop = serving.ContinuousBatcher(fe, **kw)
+    errs, finals = {}, {}
+    loop.on_error = lambda r, m: errs.setdefault(r.rid, []).append(m)
+    loop.on_chunk = lambda r, y, final: finals.__setitem__(r.rid, finals.get(r.rid, 0) + int(final))
+    clk = FakeClock()
+    return loop.run(reqs, clock=clk, sleep=clk.sleep), errs, finals
+
+
+def test_admit_failure_frees_slots_and_continues(serving):
+    """A failed admission (engine_worker.py:828-832): each of its requests gets "engine error" and its end of stream,
+    its slots are free again, and later requests are served."""
+    fe = FlakyEngine(bad_admits=(1,), B=2, buckets=(1, 2))
+    reqs = [_req(serving, 0, 0.0, cap=3), _req(serving, 1, 0.0, cap=3), _req(serving, 2, 0.5, cap=4)]
+    st, errs, finals = _run_flaky(serving, fe, reqs, admit_every=1)
+    assert errs == {0: ["engine error"], 1: ["engine error"]} and finals[0] == finals[1] == 1
+    assert reqs[0].slot == -1 and reqs[2].frames == 4 and reqs[2].slot == 0 and reqs[2].error is None
+    s = st.summary()
+    assert s["failed"] == 2 and s["finished"] == 1
+
+
+def test_tick_failure_ends_running_rows(serving):
+    """A failed tick (engine_worker.py:1186-1190) ends every running row with "engine error"; reads in flight are
+    dropped; the loop goes on with the requests that arrive later."""
+    fe = FlakyEngine(bad_ticks=(3,), B=4, buckets=(4,))
+    reqs = [_req(serving, 0, 0.0, cap=9), _req(serving, 1, 0.0, cap=9), _req(serving, 2, 1.0, cap=3)]
+    st, errs, finals = _run_flaky(serving, fe, reqs, admit_every=1)
+    assert errs == {0: ["engine error"], 1: ["engine error"]} and finals[0] == finals[1] == 1
+    assert reqs[0].frames <= 2 and reqs[0].t_done is not None
+    assert reqs[2].error is None and reqs[2].frames == 3
+    assert st.summary()["failed"] == 2
+
+
+def test_too_long_prompt_reports_error(serving):
+    fe = FakeEngine(B=2, buckets=(2,))
+    reqs = [_req(serving, 0, 0.0, cap=3, text="too long"), _req(serving, 1, 0.0, cap=3)]
+    st, errs, finals = _run_flaky(serving, fe, reqs)
+    assert errs == {0: ["text too long for TTS_MAX_SEQ"]} and finals[0] == 1 and reqs[0].rejected
+    assert st.summary()["failed"] == 0 and st.summary()["rejected"] == 1
