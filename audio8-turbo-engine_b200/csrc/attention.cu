@@ -14,6 +14,8 @@
 // (max, sum, acc) in the workspace and the last block of (r, h) (atomic ticket) merges them in split order.
 #include <algorithm>
 
+#include <atomic>
+
 #include "common.cuh"
 
 namespace a8 {
@@ -378,16 +380,31 @@ extern "C" int a8_attention_workspace(int rows, int nkv, int hd, int max_len, lo
   return A8_OK;
 }
 
+// a8_attention's argument checks, shared with a8_attention_noalloc (which runs them before it touches its array).
+static int attn_check(const void* q, int q_stride, const void* kc, const void* vc, int layers, int cache_rows,
+                      int nq, int nkv, int hd, int cache_len, int layer, const int* lens, int rows, int max_len,
+                      const void* out) {
+  if (q == nullptr || kc == nullptr || vc == nullptr || lens == nullptr || out == nullptr || rows <= 0) return A8_ERR_ARG;
+  if (nkv <= 0 || nq % nkv != 0 || layer < 0 || layer >= layers || max_len <= 0 || max_len > cache_len)
+    return A8_ERR_ARG;
+  if (hd != 64 && hd != 128) return A8_ERR_ARG;
+  const int group = nq / nkv;
+  if (!((hd == 64 && (group == 7 || group == 1)) || (hd == 128 && (group == 7 || group == 1)))) return A8_ERR_ARG;
+  if ((q_stride % 2) || (reinterpret_cast<uintptr_t>(q) & 3)) return A8_ERR_ALIGN;
+  if ((long long)layers * cache_rows * nkv * cache_len >= (1ll << 31)) return A8_ERR_SIZE;
+  if ((reinterpret_cast<uintptr_t>(kc) & 15) || (reinterpret_cast<uintptr_t>(vc) & 15)) return A8_ERR_ALIGN;
+  return A8_OK;
+}
+
 extern "C" int a8_attention(const void* q, int q_stride, const void* kc, const void* vc, int layers, int cache_rows,
                             int nq, int nkv, int hd, int cache_len, int layer, const int* lens, const int* rowmap,
                             int rows, int max_len, float scale, void* out, int out_stride, float* ws,
                             long long ws_floats, int* counters, int n_counters, a8_stream_t stream) {
-  if (q == nullptr || kc == nullptr || vc == nullptr || lens == nullptr || out == nullptr || rows <= 0) return A8_ERR_ARG;
-  if (nkv <= 0 || nq % nkv != 0 || layer < 0 || layer >= layers || max_len <= 0 || max_len > cache_len)
-    return A8_ERR_ARG;
+  int rc = attn_check(q, q_stride, kc, vc, layers, cache_rows, nq, nkv, hd, cache_len, layer, lens, rows, max_len,
+                      out);
+  if (rc) return rc;
   const int group = nq / nkv;
   const int S = attn_splits(rows, nkv, max_len);
-  if ((q_stride % 2) || (reinterpret_cast<uintptr_t>(q) & 3)) return A8_ERR_ALIGN;
   if (S > 1) {
     if (ws == nullptr || counters == nullptr || ws_floats < attn_ws_floats(rows, nkv, S, hd) ||
         n_counters < rows * nkv)
@@ -395,8 +412,7 @@ extern "C" int a8_attention(const void* q, int q_stride, const void* kc, const v
   }
   CUtensorMap mk, mv;
   const long long total = (long long)layers * cache_rows * nkv * cache_len;
-  if (total >= (1ll << 31)) return A8_ERR_SIZE;
-  int rc = attn_maps(&mk, &mv, kc, vc, total, hd);
+  rc = attn_maps(&mk, &mv, kc, vc, total, hd);
   if (rc) return rc;
   AttnArgs a;
   a.q = reinterpret_cast<const __nv_bfloat16*>(q);
@@ -422,29 +438,36 @@ extern "C" int a8_attention(const void* q, int q_stride, const void* kc, const v
 // ------------------------------------------------------------------------------------------------ allocation-free
 // a8_attention for callers that cannot allocate device memory: the split workspace (partials and tickets) lives in
 // a fixed array of this library instead of caller memory. The array is a host-side stand-in in host code; its device
-// address comes from cudaGetSymbolAddress, taken once per device with that device current, on the first call.
+// address comes from cudaGetSymbolAddress, taken once per device with that device current, on the first call there.
+// The array is sized for the largest need of any valid call (A8_ATTENTION_NOALLOC_FLOATS in the header).
 namespace a8 {
 static __device__ __align__(256) float g_attn_noalloc[A8_ATTENTION_NOALLOC_FLOATS];
-static float* g_attn_noalloc_dev[64];   // device address of g_attn_noalloc, per device ordinal
+// Device address of g_attn_noalloc per device ordinal. Threads that race on a first call store the same value; the
+// address belongs to the device's primary context and is stale after cudaDeviceReset (not re-queried).
+static std::atomic<float*> g_attn_noalloc_dev[64];
 }  // namespace a8
 
 extern "C" int a8_attention_noalloc(const void* q, int q_stride, const void* kc, const void* vc, int layers,
                                     int cache_rows, int nq, int nkv, int hd, int cache_len, int layer, const int* lens,
                                     const int* rowmap, int rows, int max_len, float scale, void* out, int out_stride,
                                     a8_stream_t stream) {
-  if (rows <= 0 || nkv <= 0 || (hd != 64 && hd != 128) || max_len <= 0) return A8_ERR_ARG;
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return A8_ERR_DEVICE;
-  if (g_attn_noalloc_dev[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_attn_noalloc) != cudaSuccess || p == nullptr) return A8_ERR_CUDA;
-    g_attn_noalloc_dev[dev] = reinterpret_cast<float*>(p);
-  }
+  // every check runs before the shared array is touched: a rejected call leaves another call's tickets alone
+  int rc = attn_check(q, q_stride, kc, vc, layers, cache_rows, nq, nkv, hd, cache_len, layer, lens, rows, max_len,
+                      out);
+  if (rc) return rc;
   const int S = attn_splits(rows, nkv, max_len);
   const long long partials = S > 1 ? attn_ws_floats(rows, nkv, S, hd) : 0;
   const long long tickets = S > 1 ? (long long)rows * nkv : 0;
   if (partials + tickets > A8_ATTENTION_NOALLOC_FLOATS) return A8_ERR_SIZE;
-  float* ws = g_attn_noalloc_dev[dev];
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return A8_ERR_DEVICE;
+  float* ws = g_attn_noalloc_dev[dev].load(std::memory_order_relaxed);
+  if (ws == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_attn_noalloc) != cudaSuccess || p == nullptr) return A8_ERR_CUDA;
+    ws = reinterpret_cast<float*>(p);
+    g_attn_noalloc_dev[dev].store(ws, std::memory_order_relaxed);
+  }
   int* counters = reinterpret_cast<int*>(ws + partials);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // the tickets must start at zero: the array keeps whatever the previous call left

@@ -10,7 +10,9 @@ segment of a row, `StreamingVocoder.snapshot`), so the files are not interchange
 """
 from __future__ import annotations
 
+import hashlib
 import os
+import re
 import zlib
 from collections import OrderedDict
 from typing import Dict, Optional
@@ -55,10 +57,18 @@ class SnapStore:
             self._pinned[k] = self._lru.pop(k)
         self._trim()
 
+    _PLAIN = re.compile(r"[A-Za-z0-9_][A-Za-z0-9_.-]{0,127}")
+
     def _file(self, key: str) -> Optional[str]:
+        """`<key>.<fp:08x>.snap` inside the directory. Voice keys come from clients: a key that is not a plain file
+        name (a path separator, `..`, a leading dot, other characters) is named by its SHA-1 instead, so no key
+        reaches outside the directory."""
         if not self.path or key not in self.fp:
             return None
-        return os.path.join(self.path, f"{key}.{self.fp[key]:08x}.snap")
+        k = str(key)
+        if not self._PLAIN.fullmatch(k) or ".." in k:
+            k = "_h" + hashlib.sha1(k.encode("utf-8", "surrogatepass")).hexdigest()[:24]
+        return os.path.join(self.path, f"{k}.{self.fp[key]:08x}.snap")
 
     def set_fp(self, key: str, fp: int):
         """The fingerprint of the codes `key`'s snapshot is (to be) made from; another one drops the stale copy."""

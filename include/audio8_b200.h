@@ -92,21 +92,24 @@ int a8_attention(const void* q, int q_stride, const void* kc, const void* vc, in
                  float scale, void* out, int out_stride, float* ws, long long ws_floats, int* counters, int n_counters,
                  a8_stream_t stream);
 
-/* Size of the library-owned workspace of a8_attention_noalloc, in 4-byte words (4 MiB). */
-#define A8_ATTENTION_NOALLOC_FLOATS (1 << 20)
+/* Size of the library-owned workspace of a8_attention_noalloc, in 4-byte words (5 MiB): the largest need of any valid
+ * call (hd 128 at rows * nkv = 295: 590 split parts x 2080 words + 295 tickets = 1,227,495 words). */
+#define A8_ATTENTION_NOALLOC_FLOATS (5 << 18)
 
 /* a8_attention without caller-provided scratch. No counterpart in the reference: it exists for callers that cannot
  * allocate device memory -- a host-language binding that is handed only the device pointers of its inputs and outputs
  * and has no CUDA allocator of its own, or a serving process whose memory pool already owns the whole device -- and
  * so cannot supply the workspace a8_attention needs when a row's keys span several splits.
- * The split partials and tickets live in one array inside this library (4 MiB, held on every device that loads the
+ * The split partials and tickets live in one array inside this library (5 MiB, held on every device that loads the
  * library until the process exits). A call needs rows * nkv * S * (16 hd + 32) + rows * nkv words of it when its rows
- * are split in S > 1 parts (S = min(16, ceil(max_len / 64), ceil(296 / (rows * nkv))), so at most about 0.65 M words);
- * a request beyond the array returns A8_ERR_SIZE.
+ * are split in S > 1 parts (S = min(16, ceil(max_len / 64), ceil(296 / (rows * nkv)))). rows * nkv * S is at most 590,
+ * so the need is at most 623,335 words at hd 64 and 1,227,495 at hd 128: every call the arguments allow fits, and
+ * A8_ERR_SIZE is only a guard. Arguments are checked before the array is touched.
  * The first call on a device looks up the array's device address (cudaGetSymbolAddress, with that device current):
- * make that first call before any stream capture. Every call shares the array and it keeps the last call's contents;
- * the tickets are cleared (cudaMemsetAsync on the given stream) at each call. Calls that overlap on the GPU (other
- * streams, other threads, the same device) race on the array. Allocates nothing. */
+ * make that first call before any stream capture; the address is not re-queried after cudaDeviceReset. Every call
+ * shares the array and it keeps the last call's contents; the tickets are cleared (cudaMemsetAsync on the given
+ * stream) at each call. Calls that overlap on the GPU (other streams, other threads, the same device) race on the
+ * array. Allocates nothing. */
 int a8_attention_noalloc(const void* q, int q_stride, const void* kc, const void* vc, int layers, int cache_rows,
                          int nq, int nkv, int hd, int cache_len, int layer, const int* lens, const int* rowmap,
                          int rows, int max_len, float scale, void* out, int out_stride, a8_stream_t stream);

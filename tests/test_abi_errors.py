@@ -92,3 +92,33 @@ def test_attention_workspace_query(lib, rows, nkv, hd, max_len):
     assert (n.value, t.value) == (need, tickets)
     assert lib.a8_attention_workspace(0, nkv, hd, max_len, C.byref(n), C.byref(t)) == ARG
     assert lib.a8_attention_workspace(rows, nkv, 96, max_len, C.byref(n), C.byref(t)) == ARG
+
+
+NOALLOC_FLOATS = 5 << 18          # A8_ATTENTION_NOALLOC_FLOATS (include/audio8_b200.h)
+
+
+def test_noalloc_array_holds_every_valid_call(lib):
+    """The allocation-free attention's fixed array covers the split workspace + tickets of every call the split rule
+    allows (host arithmetic only: any rows x kv heads, hd 64 and 128, long rows)."""
+    worst = 0
+    for hd in (64, 128):
+        for x in range(1, 400):                      # x = rows * nkv
+            s = _splits(x, 1, 1 << 16)
+            if s > 1:
+                worst = max(worst, x * s * (16 * hd + 32) + x)
+    assert worst == 1227495 and worst <= NOALLOC_FLOATS
+    for rows, nkv in ((36, 8), (147, 2), (295, 1)):
+        n, t = C.c_longlong(), C.c_int()
+        assert lib.a8_attention_workspace(rows, nkv, 128, 2048, C.byref(n), C.byref(t)) == OK
+        assert n.value + t.value <= NOALLOC_FLOATS
+
+
+def test_noalloc_rejects_before_touching_its_array(lib):
+    """Bad arguments come back as A8_ERR_ARG from the checks that run before the shared array is used (no device
+    work: every pointer here is null or the shape is unsupported)."""
+    N = None
+    assert lib.a8_attention_noalloc(N, 896, N, N, 1, 1, 14, 2, 64, 64, 0, N, N, 1, 64, 0.0, N, 896, N) == ARG
+    p = C.c_void_p(256)
+    assert lib.a8_attention_noalloc(p, 896, p, p, 1, 1, 14, 2, 96, 64, 0, p, N, 1, 64, 0.0, p, 896, N) == ARG  # hd
+    assert lib.a8_attention_noalloc(p, 896, p, p, 1, 1, 14, 2, 64, 64, 1, p, N, 1, 64, 0.0, p, 896, N) == ARG  # layer
+    assert lib.a8_attention_noalloc(p, 896, p, p, 1, 1, 14, 2, 64, 64, 0, p, N, 1, 65, 0.0, p, 896, N) == ARG  # len

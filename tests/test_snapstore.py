@@ -68,3 +68,20 @@ def test_fingerprint_change_drops_stale(ss, tmp_path):
     assert "v" not in st and st.get("v") is None
     st["v"] = _snap(2)
     assert st.on_disk() == 2 and _same(st["v"], _snap(2))
+
+
+def test_keys_stay_inside_the_directory(ss, tmp_path):
+    """Client-chosen voice keys with path separators or `..` are stored under a hashed name inside the directory."""
+    d = tmp_path / "snaps"
+    st = ss.SnapStore(str(d), ram=1)
+    for i, key in enumerate(("../escape", "a/b", "/abs", "..", ".hidden", "ok-key_1.v2")):
+        st.set_fp(key, 7 + i)
+        st[key] = _snap(i)
+    names = sorted(p.name for p in d.iterdir())
+    assert len(names) == 6 and all(p.parent == d for p in d.iterdir())
+    assert not (tmp_path / "escape.00000007.snap").exists()
+    assert "ok-key_1.v2.0000000c.snap" in names
+    st2 = ss.SnapStore(str(d), ram=1)
+    for i, key in enumerate(("../escape", "a/b", "/abs", "..", ".hidden", "ok-key_1.v2")):
+        st2.set_fp(key, 7 + i)
+        assert key in st2 and _same(st2[key], _snap(i))

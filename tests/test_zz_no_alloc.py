@@ -2,8 +2,10 @@
 only the device pointers of its inputs and outputs, a serving process whose memory pool owns the whole device). Its
 split workspace lives in an array of the library, so the caller passes inputs and outputs only.
 
-Checked through the C ABI against a8_attention (caller-owned workspace) on two calls in a row whose rows span several
-splits, so the library's array is used, and its leftovers from the first call must not leak into the second.
+Checked through the C ABI against a8_attention (caller-owned workspace) and against the CPU oracle's attention, on
+calls in a row whose rows span several splits, so the library's array is used and its leftovers from one call must
+not leak into the next: the slow AR's GQA shape (hd 64, 14 / 2 heads) and the codec's MHA shape (hd 128, 8 / 8 heads)
+at the row count with the largest workspace need.
 This file is collected last (test_zz_*): it passes alone in a fresh process and after every other test.
 """
 import pytest
@@ -21,9 +23,9 @@ def L(a8):
     return a8._lib
 
 
-def _case(seed, b, lens_hi):
+def _case(seed, b, lens_hi, nq=14, nkv=2, hd=64):
     g = torch.Generator().manual_seed(seed)
-    nq, nkv, hd, S, layers = 14, 2, 64, 2048, 2
+    S, layers = 2048, 2
     q = (torch.randn(b, nq, hd, generator=g)).to(BF).cuda()
     kc = (torch.randn(layers, b + 1, nkv, S, hd, generator=g)).to(BF).cuda()
     vc = (torch.randn(layers, b + 1, nkv, S, hd, generator=g)).to(BF).cuda()
@@ -49,8 +51,12 @@ def test_noalloc_attention_matches_workspace_version_twice(L, a8):
     import ctypes as C
     ws_floats = C.c_longlong()
     n_cnt = C.c_int()
-    for seed, b, hi in ((11, 48, 2048), (12, 37, 1300)):     # two calls in a row, different shapes and lengths
-        q, kc, vc, lens, dims = _case(seed, b, hi)
+    from oracle.ref_cpu import decode_attention
+    # calls in a row, different shapes and lengths; 36 rows x 8 heads at hd 128 = 2 splits, the largest need of the
+    # library array (36 x 8 x 2 x 2080 partial words + 288 tickets)
+    for seed, b, hi, nq, nkv, hd in ((11, 48, 2048, 14, 2, 64), (12, 37, 1300, 14, 2, 64), (13, 36, 900, 8, 8, 128),
+                                     (14, 36, 2048, 8, 8, 128)):
+        q, kc, vc, lens, dims = _case(seed, b, hi, nq, nkv, hd)
         L.check(L.load().a8_attention_workspace(b, dims[1], dims[2], dims[3], C.byref(ws_floats), C.byref(n_cnt)))
         ws = (torch.zeros(max(1, ws_floats.value), device="cuda"),
               torch.zeros(max(1, n_cnt.value), dtype=torch.int32, device="cuda"))
@@ -60,3 +66,6 @@ def test_noalloc_attention_matches_workspace_version_twice(L, a8):
         assert not torch.isnan(got.float()).any()
         rel = float((got.float() - ref.float()).abs().max() / ref.float().abs().max())
         assert rel < 1e-2, rel
+        orc = decode_attention(q.cpu().view(b, nq, hd), kc[1].cpu(), vc[1].cpu(), lens.cpu())
+        rel_o = float((got.float().cpu().view(b, nq, hd) - orc).abs().max() / orc.abs().max())
+        assert rel_o < 1e-2, rel_o
