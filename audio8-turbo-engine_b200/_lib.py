@@ -99,7 +99,8 @@ class A8Engine(C.Structure):
                 ("sil_frame", c_void_p), ("tick_ctr", c_void_p), ("tick_id", c_void_p), ("x_fast2", c_void_p),
                 ("x_fast", c_void_p), ("x_slow", c_void_p), ("codes", c_void_p), ("logits", c_void_p),
                 ("ld_logits", c_int), ("f_pos", c_void_p), ("f_pos0", c_void_p), ("f_slot0", c_void_p),
-                ("scratch", A8Scratch), ("voc", C.POINTER(A8Vocoder)), ("side", c_void_p)]
+                ("scratch", A8Scratch), ("voc", C.POINTER(A8Vocoder)), ("side", c_void_p),
+                ("rec_logits", c_void_p)]
 
 
 class A8Resample(C.Structure):

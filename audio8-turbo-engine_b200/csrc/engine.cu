@@ -135,9 +135,10 @@ static SampleArgs sample_base(const A8Engine& e) {
 static int fast_logits_and_draw(const A8Engine& e, const void* h, int ldh, int b, int i, bool next, cudaStream_t s) {
   A8Epilogue lg = {};
   lg.kind = A8_EPI_F32_ROUND;
-  A8_TRY(gemm(h, ldh, e.fast_out, e.cbk, e.H, b, e.logits, e.ld_logits, lg, e.scratch, s));
+  float* logits = e.rec_logits != nullptr ? e.rec_logits + (size_t)(i - 1) * e.B * e.ld_logits : e.logits;
+  A8_TRY(gemm(h, ldh, e.fast_out, e.cbk, e.H, b, logits, e.ld_logits, lg, e.scratch, s));
   SampleArgs sa = sample_base(e);
-  sa.logits = e.logits;
+  sa.logits = logits;
   sa.ld = e.ld_logits;
   sa.V = e.cbk;
   sa.k = (e.top_k > 0 && e.top_k < e.cbk) ? e.top_k : e.cbk;

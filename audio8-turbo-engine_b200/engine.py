@@ -259,6 +259,14 @@ class FastEngine:
     def slow_step(self, b):
         L.call("a8_slow_step", C.byref(self.desc), int(b), L.stream_handle())
 
+    def record_fast_logits(self, on=True):
+        """Keep every codebook's fast-head logits readable after a tick: `rec_logits[i - 1, r, :cbk]` (fp32) for
+        codebook i of row r (a diagnostic for tests; the head GEMM writes there instead of the shared logits buffer,
+        no extra work). A graph recorded by capture() keeps the choice it was recorded with."""
+        self.rec_logits = (torch.zeros(self.ncg - 1, self.B, self.ld_logits, dtype=torch.float32, device=self.dev)
+                           if on else None)
+        self.desc.rec_logits = L.ptr(self.rec_logits) if on else None
+
     @torch.inference_mode()
     def capture(self, log=print):
         """Warm up and record one CUDA graph per bucket (largest first)."""

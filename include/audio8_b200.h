@@ -400,6 +400,9 @@ typedef struct A8Engine {
   A8Scratch scratch;      /* for 2B rows */
   const A8Vocoder* voc;   /* host descriptor of the codec (NULL: the tick makes no audio) */
   a8_stream_t side;       /* the codec's stream (not the tick's) */
+  float* rec_logits;      /* NULL, or fp32 [ncb - 1, B, ld_logits]: codebook i's logits (i = 1 .. ncb-1) are written
+                             to slice i - 1 instead of `logits` and drawn from there, so they stay readable after the
+                             tick (a diagnostic; no extra work) */
 } A8Engine;
 
 /* One frame for slot rows [0, b): fast AR (2-token pass + ncb - 2 passes, each sampled), slow AR step, semantic

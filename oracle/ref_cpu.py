@@ -630,9 +630,10 @@ class OracleEngine:
             return logits.argmax(-1)
         return self.cb_samp(logits, self._noise(self.STREAM_CB + i, list(range(b)), self.cb_samp.k))
 
-    def fast_codes(self, hid, code0, b):
+    def fast_codes(self, hid, code0, b, forced=None):
         """serve/fast_engine.py:702-713: one 2-token pass (positions 0, 1; cache row = row) then one pass per
-        codebook."""
+        codebook. forced [b, ncg] (tests): each pass takes forced[:, i - 1] as its input code instead of the oracle's
+        own draw (teacher forcing of the fast AR; the returned codes are still the oracle's draws)."""
         x = torch.stack([hid, self.fast_emb[code0]], 1).view(2 * b, self.H)
         pos0 = torch.arange(2 * b, dtype=torch.int32) % 2
         slot0 = torch.arange(2 * b, dtype=torch.int32) // 2
@@ -645,7 +646,8 @@ class OracleEngine:
         ar = torch.arange(b, dtype=torch.int32)
         for i in range(2, self.ncg):
             pos = torch.full((b,), i, dtype=torch.int32)
-            h = self.fast.forward(self.fast_emb[c], pos, ar, pos + 1, rowmap=False)
+            cin = forced[:, i - 1] if forced is not None else c
+            h = self.fast.forward(self.fast_emb[cin], pos, ar, pos + 1, rowmap=False)
             lg = linear(h, self.fast_out)
             if self.record is not None:
                 self.record.setdefault("fast_logits", []).append(lg.clone())
@@ -658,14 +660,18 @@ class OracleEngine:
         accumulate, one rounding), then a bf16 add."""
         return bf(self.emb[sem] + bf(self.cbemb[codes + self.cb_off].sum(1)))
 
-    def tick(self, b):
-        """serve/fast_engine.py:737-769."""
+    def tick(self, b, forced=None):
+        """serve/fast_engine.py:737-769. forced [b, ncg] (tests): teacher-forced fast AR (see fast_codes); the slow
+        step then embeds the forced codes and the frame queued is the forced one."""
         t_in = self.tok[:b].clone()
         self.tok_in[:b] = t_in
         if self.voc is not None:
             self.audio[:b] = self.voc.step(self.frame_prev[:b], b)
         code0 = (t_in - self.sb).clamp(0, self.cbk - 1)
-        codes = self.fast_codes(self.hid[:b], code0, b)
+        codes = self.fast_codes(self.hid[:b], code0, b, forced)
+        if forced is not None:
+            self.record_codes = codes
+            codes = forced.clone()
         pos = self.cpos[:b].clone()
         h = self.slow.forward(self.embed(t_in, codes), pos, torch.arange(b, dtype=torch.int32), pos + 1, rowmap=False)
         logits = self._head(h)
