@@ -16,19 +16,21 @@ c_void_p, c_int, c_float, c_ll, c_ull = C.c_void_p, C.c_int, C.c_float, C.c_long
 ERRORS = {0: "ok", 1: "bad argument", 2: "CUDA call failed", 3: "TMA alignment rule broken", 4: "workspace too small",
           5: "no sm_100 device"}
 
-EPI_BF16, EPI_F32_ROUND, EPI_SILU, EPI_ROPE, EPI_GELU, EPI_LSRES = range(6)
+EPI_BF16, EPI_F32_ROUND, EPI_SILU, EPI_ROPE, EPI_GELU, EPI_LSRES, EPI_RESID = range(7)
 
 
 class A8Epilogue(C.Structure):
     _fields_ = [("kind", c_int), ("bias", c_void_p), ("cos", c_void_p), ("sin", c_void_p), ("pos", c_void_p),
                 ("slot", c_void_p), ("kc", c_void_p), ("vc", c_void_p), ("nq", c_int), ("nkv", c_int), ("hd", c_int),
-                ("ring", c_int), ("cache_len", c_int), ("gamma", c_void_p), ("res", c_void_p), ("ldres", c_int)]
+                ("ring", c_int), ("cache_len", c_int), ("gamma", c_void_p), ("res", c_void_p), ("ldres", c_int),
+                ("ssq_out", c_void_p), ("ssq_ld", c_int), ("norm_w", c_void_p), ("ssq_in", c_void_p),
+                ("eps", c_float)]
 
 
 class A8Scratch(C.Structure):
     _fields_ = [("h", c_void_p), ("q", c_void_p), ("o", c_void_p), ("a", c_void_p), ("mlp", c_void_p),
                 ("attn_ws", c_void_p), ("attn_ws_floats", c_ll), ("attn_counters", c_void_p),
-                ("n_attn_counters", c_int)]
+                ("n_attn_counters", c_int), ("ssq", c_void_p), ("ssq_ld", c_int)]
 
 
 class A8StackDesc(C.Structure):
@@ -42,7 +44,7 @@ class A8StackDesc(C.Structure):
 class A8StackRun(C.Structure):
     _fields_ = [("x", c_void_p), ("ldx", c_int), ("rows", c_int), ("pos", c_void_p), ("slot", c_void_p),
                 ("lens", c_void_p), ("lens_max", c_int), ("rowmap", c_void_p), ("max_len", c_int),
-                ("scratch", A8Scratch)]
+                ("scratch", A8Scratch), ("blocks", c_void_p), ("nblocks", c_int)]
 
 
 MAX_UPS, MAX_CONV_OPS = 4, 40
@@ -122,6 +124,8 @@ SIGNATURES = {
     "a8_attention": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                              c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_int, c_void_p, c_ll, c_void_p,
                              c_int, c_void_p]),
+    "a8_prefill_attention": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
+                                     c_int, c_void_p, c_int, c_int, c_float, c_void_p, c_int, c_void_p]),
     "a8_attention_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
                                      c_int, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_int, c_void_p]),
     "a8_rmsnorm": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_float,
@@ -150,7 +154,9 @@ SIGNATURES = {
     "a8_stack_forward": (c_int, [C.POINTER(A8StackDesc), C.POINTER(A8StackRun), c_void_p]),
     "a8_tick": (c_int, [C.POINTER(A8Engine), c_int, c_void_p]),
     "a8_slow_step": (c_int, [C.POINTER(A8Engine), c_int, c_void_p]),
-    "a8_prefill_finish": (c_int, [C.POINTER(A8Engine), c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
+    "a8_prefill_finish": (c_int, [C.POINTER(A8Engine), c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "a8_embed_prompt": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                c_void_p]),
 }
 
 _lib = None

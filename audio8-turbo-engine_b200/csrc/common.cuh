@@ -198,6 +198,16 @@ __device__ __forceinline__ float dsmem_ld(uint32_t addr) {
   return v;
 }
 
+// Generic-proxy shared-memory writes made visible to the async proxy (a tensor-core operand rewritten by threads),
+// before the barrier that hands the buffer to the MMA issuer.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// Named barrier `id` (1..15; 0 is __syncthreads) over `n` threads (a multiple of 32).
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
 // ------------------------------------------------------------------------------------------------ PDL
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

@@ -10,6 +10,8 @@ int attn_launch(const CUtensorMap& mk, const CUtensorMap& mv, AttnArgs a, int hd
 int attn_splits(int rows, int nkv, int max_len);
 long long attn_ws_floats(int rows, int nkv, int nsplit, int hd);
 int sample_launch(const SampleArgs& a, int rows, cudaStream_t s);
+int pattn_launch(const void* q, int q_stride, int rows, const CUtensorMap& mk, const CUtensorMap& mv,
+                 const PattnArgs& a, int nblocks, cudaStream_t s);
 
 #define A8_TRY(x)              \
   do {                         \
@@ -41,6 +43,13 @@ static int gemm(const void* x, int ldx, const void* w, int N, int K, int M, void
   return gemm_launch(&p, s, true);
 }
 
+// _Stack.forward (serve/fast_engine.py:117-138). With the residual stream's sums of squares in scratch (the usual
+// case: dim <= 1024), each layer is six launches -- qkv GEMM (the RMSNorm of the residual stream in its operand
+// producer, bias + RoPE + KV store in its epilogue), attention, o GEMM, residual add + RMSNorm, w13 GEMM (SiLU * up in
+// the epilogue), w2 GEMM (residual add + the rows' sums of squares in its epilogue) -- plus one RMSNorm launch at each
+// end of the stack: the first layer's input and the final-normed output in scratch.h. The w13 GEMM keeps the separate
+// RMSNorm: its 76 weight tiles would each normalise the same rows (measured slower than the launch it saves).
+// Otherwise every norm is its own launch (seven a layer), with the same arithmetic.
 int stack_forward(const A8StackDesc& d, const A8StackRun& r, cudaStream_t s) {
   const int R = r.rows, D = d.dim, QW = d.nq * d.hd, NQKV = (d.nq + 2 * d.nkv) * d.hd;
   const A8Scratch& sc = r.scratch;
@@ -50,16 +59,35 @@ int stack_forward(const A8StackDesc& d, const A8StackRun& r, cudaStream_t s) {
   __nv_bfloat16* a = reinterpret_cast<__nv_bfloat16*>(sc.a);
   __nv_bfloat16* m = reinterpret_cast<__nv_bfloat16*>(sc.mlp);
   void* res = r.x;
-  A8_TRY(a8_rmsnorm(r.x, r.ldx, nullptr, 0, d.ln1, h, D, R, D, d.eps, reinterpret_cast<a8_stream_t>(s)));
+  const bool fuse = sc.ssq != nullptr && sc.ssq_ld >= R && D <= 1024 && D % 64 == 0;
+  a8_stream_t st = reinterpret_cast<a8_stream_t>(s);
+  A8_TRY(a8_rmsnorm(r.x, r.ldx, nullptr, 0, d.ln1, h, D, R, D, d.eps, st));
   CUtensorMap mk, mv;
   const long long total = (long long)d.layers * d.cache_rows * d.nkv * d.cache_len;
   A8_TRY(attn_maps(&mk, &mv, d.kc, d.vc, total, d.hd));
   const int max_len = r.max_len > 0 ? r.max_len : d.cache_len;
-  const int ms = attn_splits(R, d.nkv, max_len);
+  // packed prefill rows with a query-block table go to the tensor-core prefill attention
+  const bool packed = r.blocks != nullptr && r.nblocks > 0 && d.hd == 64 && d.nq / d.nkv <= 8;
+  const int ms = packed ? 1 : attn_splits(R, d.nkv, max_len);
   if (ms > 1 && (sc.attn_ws == nullptr || sc.attn_ws_floats < attn_ws_floats(R, d.nkv, ms, d.hd) ||
                  sc.attn_counters == nullptr || sc.n_attn_counters < R * d.nkv))
     return A8_ERR_SIZE;
+  // an operand normalised in the GEMM's producer: the residual rows with norm weight w (RMSNorm of the stream)
+  auto normed = [&](A8Epilogue& e, const void* w) {
+    e.norm_w = w;
+    e.ssq_in = sc.ssq;
+    e.ssq_ld = sc.ssq_ld;
+    e.eps = d.eps;
+  };
+  // the residual add of rmsnorm in the epilogue, in place on the stream, with the rows' sums of squares
+  A8Epilogue resid = {};
+  resid.kind = A8_EPI_RESID;
+  resid.res = res;
+  resid.ldres = r.ldx;
+  resid.ssq_out = sc.ssq;
+  resid.ssq_ld = sc.ssq_ld;
   for (int l = 0; l < d.layers; ++l) {
+    const bool in_h = !fuse || l == 0;          // the layer's normed input is already in h
     A8Epilogue e = {};
     e.kind = A8_EPI_ROPE;
     e.bias = d.bqkv != nullptr ? at<__nv_bfloat16>(d.bqkv, l * bstride(d, 1)) : nullptr;
@@ -74,7 +102,9 @@ int stack_forward(const A8StackDesc& d, const A8StackRun& r, cudaStream_t s) {
     e.hd = d.hd;
     e.ring = d.ring > 0 ? d.ring : (1 << 30);
     e.cache_len = d.cache_len;
-    A8_TRY(gemm(h, D, at<__nv_bfloat16>(d.wqkv, l * bstride(d, 0)), NQKV, D, R, q, QW, e, sc, s));
+    if (!in_h) normed(e, at<__nv_bfloat16>(d.ln1, l * bstride(d, 5)));
+    A8_TRY(gemm(in_h ? (const void*)h : r.x, in_h ? D : r.ldx, at<__nv_bfloat16>(d.wqkv, l * bstride(d, 0)), NQKV, D,
+                R, q, QW, e, sc, s));
     AttnArgs aa = {};
     aa.q = q;
     aa.q_stride = QW;
@@ -93,20 +123,44 @@ int stack_forward(const A8StackDesc& d, const A8StackRun& r, cudaStream_t s) {
     aa.ws = sc.attn_ws;
     aa.counters = sc.attn_counters;
     aa.rows = R;
-    A8_TRY(attn_launch(mk, mv, aa, d.hd, d.nq / d.nkv, s));
+    if (packed) {
+      PattnArgs pa = {};
+      pa.blocks = r.blocks;
+      pa.nq = d.nq;
+      pa.nkv = d.nkv;
+      pa.group = d.nq / d.nkv;
+      pa.cache_len = d.cache_len;
+      pa.layer_base = aa.layer_base;
+      pa.scale_log2 = aa.scale_log2;
+      pa.out = o;
+      pa.out_stride = QW;
+      pa.rows = R;
+      A8_TRY(pattn_launch(q, QW, R, mk, mv, pa, r.nblocks, s));
+    } else {
+      A8_TRY(attn_launch(mk, mv, aa, d.hd, d.nq / d.nkv, s));
+    }
     A8Epilogue plain = {};
     plain.kind = A8_EPI_BF16;
-    A8_TRY(gemm(o, QW, at<__nv_bfloat16>(d.wo, l * bstride(d, 2)), D, QW, R, a, D, plain, sc, s));
-    A8_TRY(a8_rmsnorm(a, D, res, r.ldx, at<__nv_bfloat16>(d.ln2, l * bstride(d, 5)), h, D, R, D, d.eps,
-                      reinterpret_cast<a8_stream_t>(s)));
     A8Epilogue silu = {};
     silu.kind = A8_EPI_SILU;
-    A8_TRY(gemm(h, D, at<__nv_bfloat16>(d.w13, l * bstride(d, 3)), 2 * d.inter, D, R, m, d.inter, silu, sc, s));
-    A8_TRY(gemm(m, d.inter, at<__nv_bfloat16>(d.w2, l * bstride(d, 4)), D, d.inter, R, a, D, plain, sc, s));
-    // the next layer's normed input (or, after the last layer, the stack's final-normed output) goes to h
-    const void* nxt = l + 1 < d.layers ? at<__nv_bfloat16>(d.ln1, (l + 1) * bstride(d, 5)) : d.norm;
-    A8_TRY(a8_rmsnorm(a, D, res, r.ldx, nxt, h, D, R, D, d.eps, reinterpret_cast<a8_stream_t>(s)));
+    const void* w13 = at<__nv_bfloat16>(d.w13, l * bstride(d, 3));
+    const void* w2 = at<__nv_bfloat16>(d.w2, l * bstride(d, 4));
+    if (fuse) {
+      A8_TRY(gemm(o, QW, at<__nv_bfloat16>(d.wo, l * bstride(d, 2)), D, QW, R, a, D, plain, sc, s));
+      A8_TRY(a8_rmsnorm(a, D, res, r.ldx, at<__nv_bfloat16>(d.ln2, l * bstride(d, 5)), h, D, R, D, d.eps, st));
+      A8_TRY(gemm(h, D, w13, 2 * d.inter, D, R, m, d.inter, silu, sc, s));
+      A8_TRY(gemm(m, d.inter, w2, D, d.inter, R, res, r.ldx, resid, sc, s));
+    } else {
+      A8_TRY(gemm(o, QW, at<__nv_bfloat16>(d.wo, l * bstride(d, 2)), D, QW, R, a, D, plain, sc, s));
+      A8_TRY(a8_rmsnorm(a, D, res, r.ldx, at<__nv_bfloat16>(d.ln2, l * bstride(d, 5)), h, D, R, D, d.eps, st));
+      A8_TRY(gemm(h, D, w13, 2 * d.inter, D, R, m, d.inter, silu, sc, s));
+      A8_TRY(gemm(m, d.inter, w2, D, d.inter, R, a, D, plain, sc, s));
+      // the next layer's normed input (or, after the last layer, the stack's final-normed output) goes to h
+      const void* nxt = l + 1 < d.layers ? at<__nv_bfloat16>(d.ln1, (l + 1) * bstride(d, 5)) : d.norm;
+      A8_TRY(a8_rmsnorm(a, D, res, r.ldx, nxt, h, D, R, D, d.eps, st));
+    }
   }
+  if (fuse) A8_TRY(a8_rmsnorm(r.x, r.ldx, nullptr, 0, d.norm, h, D, R, D, d.eps, st));   // the final norm
   return A8_OK;
 }
 
@@ -268,7 +322,7 @@ int tick(const A8Engine& e, int b, cudaStream_t s) {
 // Admission tail (serve/fast_engine.py:1124-1133, :828-835): logits of each request's last prompt row -> its first
 // token (no RAS window), hidden, position; RAS window and step count cleared.
 int prefill_finish(const A8Engine& e, const void* h_last, int n, const int* slots, const int* cpos_new,
-                   cudaStream_t s) {
+                   const int* frame0, cudaStream_t s) {
   A8Epilogue lg = {};
   lg.kind = A8_EPI_F32_ROUND;
   A8_TRY(gemm(h_last, e.H, e.head, e.nsem + 1, e.H, n, e.logits, e.ld_logits, lg, e.scratch, s));
@@ -288,6 +342,9 @@ int prefill_finish(const A8Engine& e, const void* h_last, int n, const int* slot
   sa.hid = reinterpret_cast<__nv_bfloat16*>(e.hid);
   sa.st = slots;
   sa.cpos_new = cpos_new;
+  sa.frame0 = frame0;
+  sa.frame_prev = e.frame_prev;
+  sa.B = e.B;
   sa.tick_id = e.tick_ctr;            // draws between ticks use the count of ticks run so far
   return sample_launch(sa, n, s);
 }
@@ -305,10 +362,9 @@ extern "C" int a8_slow_step(const A8Engine* e, int b, a8_stream_t stream) {
 }
 
 extern "C" int a8_prefill_finish(const A8Engine* e, const void* h_last, int n, const int* slots, const int* cpos_new,
-                                 a8_stream_t stream) {
-  if (e == nullptr || h_last == nullptr || slots == nullptr || cpos_new == nullptr || n <= 0 || n > e->B)
-    return A8_ERR_ARG;
-  return prefill_finish(*e, h_last, n, slots, cpos_new, reinterpret_cast<cudaStream_t>(stream));
+                                 const int* frame0, a8_stream_t stream) {
+  if (e == nullptr || h_last == nullptr || slots == nullptr || cpos_new == nullptr || n <= 0) return A8_ERR_ARG;
+  return prefill_finish(*e, h_last, n, slots, cpos_new, frame0, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int a8_stack_forward(const A8StackDesc* d, const A8StackRun* r, a8_stream_t stream) {

@@ -31,11 +31,29 @@ constexpr int STAGE_PITCH = 132;        // fp32 epilogue staging row pitch (bank
 constexpr int KERNEL_ID_GEMM = 1;
 constexpr int GEMM_PARTS = 4;           // warps per TMEM lane quarter in the epilogue
 constexpr int GEMM_THREADS = 128 * GEMM_PARTS;
+constexpr int NORM_WARP0 = 2;           // warps 2-15 normalise X tiles during the mainloop (operand RMSNorm)
+constexpr int NORM_WARPS = GEMM_THREADS / 32 - NORM_WARP0;
+constexpr int NORM_MAX_K = 1024;
+// operand-normalisation shared memory: normed barriers (<= 8), rstd[256], norm weight[NORM_MAX_K] (bf16)
+constexpr int NORM_SMEM = 8 * 8 + 16 + 256 * 4 + NORM_MAX_K * 2;   // (+16: alignment of rstd)
 
 struct EpiCtx {
   const GemmArgs* a;
   int n0, m_base;
 };
+
+// ------------------------------------------------------------------------------------------------ operand norm
+// bf16 pair (x0, x1) -> bf16 pair (bf16(x0 * r), bf16(x1 * r)), the products in fp32
+__device__ __forceinline__ uint32_t scale_bf16x2(uint32_t u, float r) {
+  const float2 f = unpack_bf16(u);
+  return pack_bf16(f.x * r, f.y * r);
+}
+// bf16 pairs multiplied lane-wise, each product rounded to nearest once
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 
 // ------------------------------------------------------------------------------------------------ epilogues
 // 8 bf16 (16-byte aligned) -> fp32
@@ -129,6 +147,57 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, const float* s
       for (int i = 0; i < 32; ++i)
         if (nb + i < a.N) y[nb + i] = __float2bfloat16_rn(o[i]);
     }
+  } else if constexpr (KIND == A8_EPI_RESID) {
+    // rmsnorm's residual add (serve/fast_kernels.py:36-40): y = bf16(bf16(acc + bias) + res), and this tile's part
+    // of the row's sum of squares of y for the next GEMM's operand normalisation
+    const __nv_bfloat16* bias = reinterpret_cast<const __nv_bfloat16*>(e.bias);
+    const __nv_bfloat16* res = reinterpret_cast<const __nv_bfloat16*>(e.res) + (size_t)m * e.ldres;
+    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(a.y) + (size_t)m * a.ldy;
+    float o[32];
+    const bool vec = nb + 32 <= a.N &&
+                     ((reinterpret_cast<uintptr_t>(y + nb) | reinterpret_cast<uintptr_t>(res + nb) |
+                       (bias != nullptr ? reinterpret_cast<uintptr_t>(bias + nb) : 0)) & 15) == 0;
+    if (vec) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float rx[8], bx[8];
+        load8_bf16(res + nb + 8 * q, rx);
+        if (bias != nullptr) {
+          load8_bf16(bias + nb + 8 * q, bx);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) bx[k] = 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[8 * q + k] = bf16r(bf16r(v[8 * q + k] + bx[k]) + rx[k]);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(y + nb);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        dst[q] = make_uint4(pack_bf16(o[8 * q], o[8 * q + 1]), pack_bf16(o[8 * q + 2], o[8 * q + 3]),
+                            pack_bf16(o[8 * q + 4], o[8 * q + 5]), pack_bf16(o[8 * q + 6], o[8 * q + 7]));
+    } else {
+      for (int i = 0; i < 32; ++i) {
+        const int n = nb + i;
+        o[i] = 0.f;
+        if (n < a.N) {
+          const float b = bias != nullptr ? __bfloat162float(bias[n]) : 0.f;
+          o[i] = bf16r(bf16r(v[i] + b) + __bfloat162float(res[n]));
+        }
+      }
+      for (int i = 0; i < 32; ++i)
+        if (nb + i < a.N) y[nb + i] = __float2bfloat16_rn(o[i]);
+    }
+    if (e.ssq_out != nullptr) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) ss += o[i] * o[i];
+      // the four 32-column segments of this token sit in lanes 4j .. 4j+3 (all present or all gone)
+      const unsigned quad = 0xFu << (threadIdx.x & 28);
+      ss += __shfl_xor_sync(quad, ss, 1);
+      ss += __shfl_xor_sync(quad, ss, 2);
+      if (seg == 0) e.ssq_out[(size_t)(n0 >> 7) * e.ssq_ld + m] = ss;
+    }
   } else if constexpr (KIND == A8_EPI_F32_ROUND) {
     float* y = reinterpret_cast<float*>(a.y) + (size_t)m * a.ldy;
     if (nb + 32 <= a.N && ((reinterpret_cast<uintptr_t>(y + nb) & 15) == 0)) {
@@ -155,11 +224,13 @@ __device__ __forceinline__ void epilogue_silu(const GemmArgs& a, const float* st
   const int I = a.N / 2;
   __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(a.y) + (size_t)m * a.ldy;
   float o[16];
+  // silu(g) = g / (1 + exp(-g)) with the approximate exponential and divide the reference's Triton kernel compiles to
+  // (tl.exp, fp32 '/'; serve/fast_kernels.py:531-533), rounded to bf16 before the product
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const float gv = bf16r(g[i]);
     const float uv = bf16r(u[i]);
-    const float gs = bf16r(gv / (1.0f + expf(-gv)));
+    const float gs = bf16r(__fdividef(gv, 1.0f + __expf(-gv)));
     o[i] = gs * uv;
   }
   if (c0 + 16 <= I && ((reinterpret_cast<uintptr_t>(y + c0) & 15) == 0)) {
@@ -281,6 +352,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint64_t* accum = empty + stages;
   uint64_t* recv_bar = accum + 1;         // split-K: the peers' partials have all landed in recv
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv_bar + 1);
+  // operand normalisation: a stage's X tile normalised in place (normed[s]), per-token 1/rms, the norm weight
+  const bool norm = a.epi.norm_w != nullptr;
+  uint64_t* normed = recv_bar + 2;
+  // (16-byte aligned: the norm weight is read as 16-byte vectors)
+  float* rstd_s = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(normed + stages) + 15) & ~uintptr_t(15));
+  uint32_t* normw_s = reinterpret_cast<uint32_t*>(rstd_s + 256);   // bf16 pairs
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile_n = blockIdx.x, tile_m = blockIdx.y, split = blockIdx.z;
@@ -297,6 +374,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     mbar_init(accum, 1);
     mbar_init(recv_bar, 1);
+    for (int s = 0; s < stages; ++s) mbar_init(&normed[s], NORM_WARPS);
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, a.tmem_cols);
@@ -340,7 +418,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const uint32_t idesc = umma_idesc(128, a.ntok, 1);
       for (int i = 0; i < nkb; ++i) {
         const int s = i % stages;
-        if (!mbar_wait(&full[s], (i / stages) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_GEMM)) break;
+        if (!mbar_wait(norm ? &normed[s] : &full[s], (i / stages) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_GEMM)) break;
         tc_fence_after();
         const uint64_t da = umma_desc_sw128(tileA(s)), db = umma_desc_sw128(tileB(s));
 #pragma unroll
@@ -348,6 +426,46 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         umma_commit(&empty[s]);
       }
       umma_commit(accum);
+    }
+  } else if (norm && warp >= NORM_WARP0 && warp < NORM_WARP0 + NORM_WARPS) {
+    // RMSNorm of the X rows (serve/fast_kernels.py:41-45): row m of every stage's tile becomes
+    // bf16(w * bf16(x * rstd[m])), rstd from the row's partial sums of squares added in tile order. The tile is
+    // 128B-swizzled: 16-byte chunk pc of row m holds K elements 8 (pc ^ (m % 8)) .. +7 of the stage's 64.
+    const int nt = tid - NORM_WARP0 * 32;
+    const uint32_t* nw = reinterpret_cast<const uint32_t*>(a.epi.norm_w);
+    for (int k = nt; k < a.K / 2; k += NORM_WARPS * 32) normw_s[k] = nw[k];
+    pdl_wait();                                 // the partial sums are the previous kernel's output
+    const int tiles = (a.K + 127) / 128;
+    for (int j = nt; j < a.ntok; j += NORM_WARPS * 32) {
+      const int m = m0 + j;
+      float r = 0.f;
+      if (m < a.M) {
+        float ss = 0.f;
+        for (int t = 0; t < tiles; ++t) ss += a.epi.ssq_in[(size_t)t * a.epi.ssq_ld + m];
+        r = rsqrtf(ss / (float)a.K + a.epi.eps);
+      }
+      rstd_s[j] = r;
+    }
+    named_bar_sync(1, NORM_WARPS * 32);
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % stages;
+      if (!mbar_wait(&full[s], (i / stages) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_GEMM)) break;
+      uint8_t* tb = tileB(s);
+      const uint4* wk0 = reinterpret_cast<const uint4*>(normw_s + (kb0 + i) * (BK / 2));
+      for (int c = nt; c < a.ntok * 8; c += NORM_WARPS * 32) {
+        const int m = c >> 3, pc = c & 7;
+        const uint4 wq = wk0[pc ^ (m & 7)];
+        uint4* p = reinterpret_cast<uint4*>(tb + m * 128 + pc * 16);
+        const uint4 u = *p;
+        const float rs = rstd_s[m];
+        // bf16(w * bf16(x * rs)): the product of two bf16 values is exact in fp32, so one bf16x2 multiply rounds it
+        // exactly as the fp32 product rounded to bf16
+        *p = make_uint4(bf16x2_mul(scale_bf16x2(u.x, rs), wq.x), bf16x2_mul(scale_bf16x2(u.y, rs), wq.y),
+                        bf16x2_mul(scale_bf16x2(u.z, rs), wq.z), bf16x2_mul(scale_bf16x2(u.w, rs), wq.w));
+      }
+      fence_proxy_async_smem();                 // the tensor core reads these generic-proxy writes
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&normed[s]);
     }
   }
   __syncwarp();
@@ -512,7 +630,8 @@ static const void* gemm_fn(int kind) {
     case A8_EPI_SILU: return (const void*)k_gemm<A8_EPI_SILU>;
     case A8_EPI_ROPE: return (const void*)k_gemm<A8_EPI_ROPE>;
     case A8_EPI_GELU: return (const void*)k_gemm<A8_EPI_GELU>;
-    default: return (const void*)k_gemm<A8_EPI_LSRES>;
+    case A8_EPI_LSRES: return (const void*)k_gemm<A8_EPI_LSRES>;
+    default: return (const void*)k_gemm<A8_EPI_RESID>;
   }
 }
 
@@ -567,15 +686,15 @@ static int num_sms() {
 // Shared memory of a (ntok, splits) configuration: pipeline slots, and for split-K the receive buffer of
 // S x 128 x wp fp32 plus the reduced slice (as the kernel lays them out). Returns the stage count, or 0 if it does
 // not fit in 227 KB.
-static int size_config(int ntok, int S, int kb_per_split, int* smem) {
+static int size_config(int ntok, int S, int kb_per_split, int extra, int* smem) {
   const int stage_bytes = TILE_A_BYTES + ntok * BK * 2;
   const int ntok32 = (ntok + 31) / 32 * 32;
   const int w = ((ntok32 + S - 1) / S + 3) / 4 * 4;
   const int wp = w % 32 ? w : w + 4;
   const int reduce_bytes = S > 1 ? S * 128 * wp * 4 + 32 * STAGE_PITCH * 4 : 0;
-  int stages = std::max(2, std::min(8, (200 * 1024 - reduce_bytes) / stage_bytes));
+  int stages = std::max(2, std::min(8, (200 * 1024 - reduce_bytes - extra) / stage_bytes));
   stages = std::min(stages, std::max(2, kb_per_split));
-  *smem = stages * stage_bytes + reduce_bytes + 1024 + 256;
+  *smem = stages * stage_bytes + reduce_bytes + 1024 + 256 + extra;
   return *smem <= 227 * 1024 ? stages : 0;
 }
 
@@ -583,7 +702,7 @@ static int size_config(int ntok, int S, int kb_per_split, int* smem) {
 // 256 balanced rows; otherwise every (token tile 32..256, splits 1..16) is scored by a launch-time model fitted to
 // measured times of the tick's GEMM shapes on B200 -- waves of resident CTAs (or clusters) x (per K block cost
 // growing with the tile + a fixed cost), plus the split-K exchange -- and the cheapest is kept (cached per shape).
-static void choose(int kind, int N, int K, int M, int splits_req, int* ntok, int* splits) {
+static void choose(int kind, int N, int K, int M, int splits_req, int extra, int* ntok, int* splits) {
   const int kb_total = (K + BK - 1) / BK;
   if (splits_req > 0) {
     *ntok = pick_ntok(M);
@@ -592,7 +711,7 @@ static void choose(int kind, int N, int K, int M, int splits_req, int* ntok, int
   }
   static std::mutex mu;
   static std::unordered_map<long long, long long> cache;
-  const long long key = ((long long)kind << 56) | ((long long)N << 36) | ((long long)K << 18) | M;
+  const long long key = ((long long)(kind + 8 * (extra > 0)) << 56) | ((long long)N << 36) | ((long long)K << 18) | M;
   {
     std::lock_guard<std::mutex> g(mu);
     auto f = cache.find(key);
@@ -621,7 +740,7 @@ static void choose(int kind, int N, int K, int M, int splits_req, int* ntok, int
       const int kps = (kb_total + s - 1) / s, S = (kb_total + kps - 1) / kps;
       if (S != s) continue;
       int smem = 0;
-      if (size_config(per, S, kps, &smem) == 0) continue;
+      if (size_config(per, S, kps, extra, &smem) == 0) continue;
       const int cap = S == 1 ? sms : max_clusters(kind, smem, S);
       if (cap <= 0) continue;
       const int waves = (tiles + cap - 1) / cap;
@@ -645,7 +764,14 @@ int gemm_plan(GemmPlan* p, const void* x, int ldx, const void* w, int N, int K, 
               const A8Epilogue* epi, int splits) {
   std::memset(p, 0, sizeof(*p));
   if (x == nullptr || w == nullptr || y == nullptr || epi == nullptr || N <= 0 || K <= 0 || M <= 0) return A8_ERR_ARG;
-  if (epi->kind < A8_EPI_BF16 || epi->kind > A8_EPI_LSRES) return A8_ERR_ARG;
+  if (epi->kind < A8_EPI_BF16 || epi->kind > A8_EPI_RESID) return A8_ERR_ARG;
+  if (epi->kind == A8_EPI_RESID && (epi->res == nullptr || (epi->ssq_out != nullptr && epi->ssq_ld < M)))
+    return A8_ERR_ARG;
+  const bool norm = epi->norm_w != nullptr;
+  if (norm && (epi->ssq_in == nullptr || epi->ssq_ld < M || K > NORM_MAX_K || K % BK != 0 || !(epi->eps >= 0.f)))
+    return A8_ERR_ARG;
+  if (norm && (reinterpret_cast<uintptr_t>(epi->norm_w) & 3)) return A8_ERR_ALIGN;   // read as bf16 pairs
+  const int extra = norm ? NORM_SMEM : 0;
   if (epi->kind == A8_EPI_SILU && (N % 128) != 0) return A8_ERR_ARG;
   if (epi->kind == A8_EPI_ROPE && (epi->hd != 64 && epi->hd != 128)) return A8_ERR_ARG;
   if (epi->kind == A8_EPI_ROPE && (N != (epi->nq + 2 * epi->nkv) * epi->hd || epi->pos == nullptr ||
@@ -654,7 +780,7 @@ int gemm_plan(GemmPlan* p, const void* x, int ldx, const void* w, int N, int K, 
     return A8_ERR_ARG;
   if (epi->kind == A8_EPI_LSRES && (epi->res == nullptr || epi->gamma == nullptr)) return A8_ERR_ARG;
   GemmArgs& a = p->args;
-  choose(epi->kind, N, K, M, splits, &a.ntok, &a.splits);
+  choose(epi->kind, N, K, M, splits, extra, &a.ntok, &a.splits);
   a.n_tiles = (N + 127) / 128;
   a.tok_tiles = (M + a.ntok - 1) / a.ntok;
   a.kb_total = (K + BK - 1) / BK;
@@ -676,9 +802,9 @@ int gemm_plan(GemmPlan* p, const void* x, int ldx, const void* w, int N, int K, 
     const int w = ((ntok32 + a.splits - 1) / a.splits + 3) / 4 * 4;
     const int wp = w % 32 ? w : w + 4;
     const int reduce_bytes = a.splits > 1 ? a.splits * 128 * wp * 4 + 32 * STAGE_PITCH * 4 : 0;
-    a.stages = std::max(2, std::min(8, (budget - reduce_bytes) / stage_bytes));
+    a.stages = std::max(2, std::min(8, (budget - reduce_bytes - extra) / stage_bytes));
     a.stages = std::min(a.stages, std::max(2, a.kb_per_split));
-    smem = a.stages * stage_bytes + reduce_bytes + 1024 + 256;
+    smem = a.stages * stage_bytes + reduce_bytes + 1024 + 256 + extra;
     const bool fits = smem <= 227 * 1024 && (a.splits == 1 || cluster_fits(epi->kind, smem, a.splits));
     if (fits || a.splits == 1) break;
     const int s = std::max(1, a.splits / 2);         // a cluster that cannot be resident: halve it
@@ -734,6 +860,7 @@ int gemm_launch(const GemmPlan* p, cudaStream_t s, bool pdl) {
     case A8_EPI_ROPE: e = launch_kind<A8_EPI_ROPE>(p, s, pdl); break;
     case A8_EPI_GELU: e = launch_kind<A8_EPI_GELU>(p, s, pdl); break;
     case A8_EPI_LSRES: e = launch_kind<A8_EPI_LSRES>(p, s, pdl); break;
+    case A8_EPI_RESID: e = launch_kind<A8_EPI_RESID>(p, s, pdl); break;
     default: return A8_ERR_ARG;
   }
   return e == cudaSuccess ? A8_OK : A8_ERR_CUDA;

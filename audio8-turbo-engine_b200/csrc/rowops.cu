@@ -104,6 +104,41 @@ __global__ void k_embed_frame(const int64_t* __restrict__ sem, const int64_t* __
   }
 }
 
+// Packed prompt rows (serve/fast_engine.py:941-945, _prompt_embeds): ids[r] = (sem, audio, code_0 .. code_{ncb-1})
+// (int32): x[r] = emb[sem] on text positions, bf16(emb[sem] + bf16(sum_k cbemb[code_k + cbk k])) on audio positions
+// (the codebook sum in fp32, k in order, rounded once).
+__global__ void k_embed_prompt(const int* __restrict__ ids, int ncb, int cbk, const __nv_bfloat16* __restrict__ emb,
+                               const __nv_bfloat16* __restrict__ cbemb, __nv_bfloat16* __restrict__ x, int ldx,
+                               int rows, int H, int vocab) {
+  pdl_launch();
+  pdl_wait();
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int* id = ids + (size_t)row * (2 + ncb);
+  int s = id[0];
+  s = s < 0 ? 0 : (s >= vocab ? vocab - 1 : s);
+  const bool audio = id[1] != 0;
+  for (int c = lane * 8; c < H; c += 256) {
+    float e0[8];
+    ld8(emb + (size_t)s * H + c, e0);
+    if (audio) {
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int k = 0; k < ncb; ++k) {
+        int cd = id[2 + k];
+        cd = cd < 0 ? 0 : (cd >= cbk ? cbk - 1 : cd);
+        float e[8];
+        ld8(cbemb + ((size_t)k * cbk + cd) * H + c, e);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] += e[i];
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) e0[i] += bf16r(acc[i]);
+    }
+    st8(x + (size_t)row * ldx + c, e0);
+  }
+}
+
 // Tick start (serve/fast_engine.py:742-749, :705): tok_in = tok; code0 = clamp(tok - sb, 0, cbk-1) into codes[:, 0];
 // the fast AR's 2-token rows x[2r] = hid[r], x[2r+1] = fast_emb[code0]; block 0 also draws this tick's number
 // from the counter (tick_id[0] = ctr[0]++).
@@ -189,6 +224,20 @@ extern "C" int a8_embed_frame(const int64_t* sem, const int64_t* codes, int ncb,
   __nv_bfloat16* xp = reinterpret_cast<__nv_bfloat16*>(x);
   void* args[] = {&sem, &codes, &ncb, &cbk, &ep, &cp, &xp, &ldx, &rows, &H, &vocab};
   return launch_pdl((const void*)k_embed_frame, dim3((rows + 3) / 4), dim3(128), args,
+                    reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess ? A8_OK : A8_ERR_CUDA;
+}
+
+extern "C" int a8_embed_prompt(const int* ids, int ncb, int cbk, const void* emb, const void* cbemb, void* x, int ldx,
+                               int rows, int H, int vocab, a8_stream_t stream) {
+  if (ids == nullptr || emb == nullptr || cbemb == nullptr || x == nullptr || rows <= 0 || (H % 8) || ncb < 0 ||
+      cbk <= 0 || vocab <= 0)
+    return A8_ERR_ARG;
+  if ((ldx % 8) || (reinterpret_cast<uintptr_t>(x) & 15)) return A8_ERR_ALIGN;
+  const __nv_bfloat16* ep = reinterpret_cast<const __nv_bfloat16*>(emb);
+  const __nv_bfloat16* cp = reinterpret_cast<const __nv_bfloat16*>(cbemb);
+  __nv_bfloat16* xp = reinterpret_cast<__nv_bfloat16*>(x);
+  void* args[] = {&ids, &ncb, &cbk, &ep, &cp, &xp, &ldx, &rows, &H, &vocab};
+  return launch_pdl((const void*)k_embed_prompt, dim3((rows + 3) / 4), dim3(128), args,
                     reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess ? A8_OK : A8_ERR_CUDA;
 }
 

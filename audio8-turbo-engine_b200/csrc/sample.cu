@@ -51,6 +51,8 @@ struct SampleArgs {
   int nsem;
   const int* st;         // prefill: slot of each row
   const int* cpos_new;   // prefill: position after the prompt
+  const int* frame0;     // prefill: int32 [rows, ncb] the codec frame each slot decodes first (or null)
+  int B;                 // prefill: slots; a row aimed at slot >= B (a graph's padding) writes nothing
   int64_t* out_tok;      // plain mode: the drawn index
 };
 
@@ -193,6 +195,8 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const SampleArgs a) {
   pdl_launch();
   pdl_wait();
   const int row = blockIdx.x, tid = threadIdx.x;
+  // a prefill graph's padding request (slot B, the scratch row) draws nothing (uniform over the block)
+  if (a.mode == SM_PREFILL && (a.st[row] < 0 || a.st[row] >= a.B)) return;
   const int V = a.V;
   const float* lg = a.logits + (size_t)row * a.ld;
   for (int i = tid; i < V; i += SAMPLE_THREADS) s_x[i] = lg[i];
@@ -375,12 +379,15 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const SampleArgs a) {
           t_in == a.eos ? a.sil_frame[tid] : a.codes[(size_t)row * a.ncb + tid];
   } else {  // SM_PREFILL
     const int slot = a.st[row];
+    if (slot < 0 || slot >= a.B) return;       // a graph's padding request (the scratch slot): no state to write
     if (tid == 0) {
       a.tok[slot] = j1 == a.nsem ? a.eos : j1 + a.sb;
       a.cpos[slot] = a.cpos_new[row];
       a.nstep[slot] = 0;
     }
     if (tid < a.ras_w) a.prev[(size_t)slot * a.ras_w + tid] = 0;
+    if (a.frame0 != nullptr && tid < a.ncb)
+      a.frame_prev[(size_t)slot * a.ncb + tid] = a.frame0[(size_t)row * a.ncb + tid];
     for (int c = tid * 8; c < a.H; c += SAMPLE_THREADS * 8)
       *reinterpret_cast<uint4*>(a.hid + (size_t)slot * a.H + c) =
           *reinterpret_cast<const uint4*>(a.h_src + (size_t)row * a.ldh + c);

@@ -7,7 +7,9 @@ Same constructor, attributes and methods as the reference (serve/fast_engine.py:
 PyTorch only allocates device memory and provides streams and CUDA graphs here. Every kernel of the tick and of
 admission is a hand-written sm_100a kernel in libaudio8_b200.so, reached through its C ABI (include/audio8_b200.h):
 ``a8_tick`` launches one whole frame (fast AR, slow AR, sampling, state update), recorded once per bucket into a
-CUDA graph; ``a8_stack_forward`` + ``a8_prefill_finish`` run the packed prefill of an admission.
+CUDA graph; an admission chunk is one copy of int32 metadata and one replay of a prefill graph per token bucket
+(``a8_embed_prompt`` -> ``a8_stack_forward`` with the tensor-core packed attention -> ``a8_gather_rows`` ->
+``a8_prefill_finish``), after the voices' cached prefix K/V and codec state are loaded with ``a8_state_rows``.
 """
 from __future__ import annotations
 
@@ -111,10 +113,12 @@ class Scratch:
         L.check(L.load().a8_attention_workspace(rows, nkv, hd, max_len, C.byref(n), None), "attention workspace")
         self.attn_ws = torch.zeros(max(1, n.value), dtype=torch.float32, device=dev)
         self.attn_counters = torch.zeros(rows * nkv, dtype=torch.int32, device=dev)
+        self.ssq = torch.zeros(8, rows, dtype=torch.float32, device=dev)
         self.desc = L.A8Scratch(
             h=L.ptr(self.h), q=L.ptr(self.q), o=L.ptr(self.o), a=L.ptr(self.a), mlp=L.ptr(self.mlp),
             attn_ws=L.ptr(self.attn_ws), attn_ws_floats=self.attn_ws.numel(), attn_counters=L.ptr(self.attn_counters),
-            n_attn_counters=self.attn_counters.numel())
+            n_attn_counters=self.attn_counters.numel(), ssq=L.ptr(self.ssq), ssq_ld=rows)
+        self.rows = rows
 
 
 class FastEngine:
@@ -222,6 +226,18 @@ class FastEngine:
         self.pf_st = torch.zeros(self.pf_rows, dtype=i32, device=dev)
         self.pf_cpos = torch.zeros(self.pf_rows, dtype=i32, device=dev)
         self.pf_hl = torch.zeros(max(B, 64), H, dtype=BF16, device=dev)
+        self.pf_blocks = torch.zeros(self.pf_rows // 64 + B + 2, 4, dtype=i32, device=dev)
+        # prefill graphs: one per token bucket (64, 128, ... up to pf_rows), up to pf_NR requests a chunk, fed by one
+        # int32 metadata buffer (serve/fast_engine.py:682-691 pf_meta, :797-812); TTS_PREFILL_GRAPHS=0: the same
+        # launches eagerly
+        self.pf_buckets = sorted({64 << k for k in range(16) if (64 << k) <= self.pf_rows} | {self.pf_rows})
+        self.pf_NT, self.pf_NR = self.pf_buckets[-1], 64
+        self.pf_graph_on = os.environ.get("TTS_PREFILL_GRAPHS", "1").strip().lower() not in ("0", "false", "no", "off")
+        self.pf_graphs: Dict[int, torch.cuda.CUDAGraph] = {}
+        self.pf_off = self._pf_layout()
+        self.pf_meta = torch.zeros(int(self.pf_off[-1]), dtype=i32, device=dev)
+        self.pf_meta_h = torch.zeros(int(self.pf_off[-1]), dtype=i32).pin_memory()
+        self.pf_x = torch.zeros(self.pf_rows, H, dtype=BF16, device=dev)
 
         self.desc = L.A8Engine(
             B=B, S=self.S, H=H, ncb=self.ncg, cbk=self.cbk, nsem=self.nsem, vocab=self.emb.shape[0], ras_w=self.ras_w,
@@ -286,8 +302,10 @@ class FastEngine:
                 self.tick(b)
             self.graphs[b] = g
         torch.cuda.synchronize()
+        self.capture_prefill(log)
         self.reset_state()
-        log(f"[a8] captured {len(self.graphs)} tick graphs {self.buckets} in {time.perf_counter() - t0:.1f}s")
+        log(f"[a8] captured {len(self.graphs)} tick graphs {self.buckets} + {len(self.pf_graphs)} prefill graphs "
+            f"{sorted(self.pf_graphs)} in {time.perf_counter() - t0:.1f}s")
 
     def reset_state(self):
         for t in (self.tok, self.cpos, self.hid, self.prev, self.nstep, self.tick_ctr, self.frame_prev, self.audio):
@@ -361,28 +379,32 @@ class FastEngine:
         aud[len(head):len(head) + T] = True
         return sem, cb, aud
 
-    def _prompt_embeds(self, sem, cb, aud):
-        """Slow AR input embeds [L, H]: codebook sum on audio positions only (serve/fast_engine.py:941-945)."""
-        sem, cb, aud = (t.to(self.dev) for t in (sem, cb, aud))
-        e = self.emb[sem]
-        full = (e.float() + self.cbemb[cb + self.cb_off].float().sum(1).to(BF16).float()).to(BF16)
-        return torch.where(aud.unsqueeze(1), full, e)
+    def _prompt_rows(self, sem, cb, aud):
+        """Prompt positions as the int32 rows a8_embed_prompt reads: (sem, audio, code_0 .. code_{ncg-1}) -- the
+        codebook sum is added on audio positions only (serve/fast_engine.py:941-945)."""
+        rows = np.zeros((len(sem), 2 + self.ncg), dtype=np.int32)
+        rows[:, 0] = np.asarray(sem, dtype=np.int64)
+        rows[:, 1] = np.asarray(aud, dtype=np.int64)
+        rows[:, 2:] = np.asarray(cb, dtype=np.int64).reshape(len(sem), self.ncg)
+        return rows
 
     def _speaker_prefix(self, key, item):
         hit = self._spk_cache.get(key)
         if hit is None:
-            hit = self._prompt_embeds(*self._prompt_ids(item))
+            sem, cb, aud = self._prompt_ids(item)
+            hit = self._prompt_rows(sem.numpy(), cb.numpy(), aud.numpy())
             self._spk_cache[key] = hit
         return hit
 
     @torch.inference_mode()
     def build_prompts(self, reqs):
+        """(key, voice-prefix rows, rest rows) per request; rows as _prompt_rows (host int32)."""
         if not reqs:
             return []
         if self._parts is None:
             self._parts_init()
         P = self._parts
-        sems, cbs, auds = [], [], []
+        out = []
         for r in reqs:
             ctx_t = (r.get("ctx_text") or "").strip()
             ids = torch.tensor(self._enc(_clean_text((ctx_t + " " if ctx_t else "") + r["text"]) or ".") + P.tail,
@@ -394,10 +416,9 @@ class FastEngine:
                 ids = torch.cat([ids, cc[:, 0] + self.sb])
                 cb = torch.cat([cb, cc])
                 aud = torch.cat([aud, torch.ones(len(cc), dtype=torch.bool)])
-            sems.append(ids), cbs.append(cb), auds.append(aud)
-        lens = [len(t) for t in sems]
-        rest_e = torch.split(self._prompt_embeds(torch.cat(sems), torch.cat(cbs), torch.cat(auds)), lens)
-        return [(r["key"], self._speaker_prefix(r["key"], r["item"]), rest_e[i]) for i, r in enumerate(reqs)]
+            rest = self._prompt_rows(ids.numpy(), cb.numpy(), aud.numpy())
+            out.append((r["key"], self._speaker_prefix(r["key"], r["item"]), rest))
+        return out
 
     # ------------------------------------------------------------------ admission (serve/fast_engine.py:1035-1156)
     def evict_voices(self, keys) -> int:
@@ -409,8 +430,8 @@ class FastEngine:
         return n
 
     def voice_state_bytes(self) -> int:
-        n = sum(t.numel() * t.element_size() for kv in self._pkv.values() for t in kv)
-        return n + sum(t.numel() * t.element_size() for t in self._spk_cache.values())
+        n = sum(e.blob.numel() + e.segs.numel() for e in self._pkv.values())
+        return n + sum(t.nbytes for t in self._spk_cache.values())
 
     def prime_speaker(self, key, item):
         self.prime_speakers([(key, item)])
@@ -456,32 +477,173 @@ class FastEngine:
                 self.voc_snaps[key] = ([t.cpu().pin_memory() for t in snaps[r]], last.cpu())
             self.voc.clear_many(list(range(n)))
 
-    def _forward_rows(self, x, pos, slot, max_len):
-        """Packed causal prefill of rows x [n, H] (bf16, consumed) at positions pos into cache rows slot."""
+    @staticmethod
+    def query_blocks(pos, slot, bm=64):
+        """The packed-prefill query blocks (q0, n, slot, pos0) of rows at host positions `pos` in cache rows `slot`:
+        runs of consecutive positions of one cache row, at most `bm` rows each (PrefillPlan's blocks,
+        serve/fast_kernels.py:335-347)."""
+        pos, slot = np.asarray(pos, dtype=np.int64), np.asarray(slot, dtype=np.int64)
+        out, i, n = [], 0, len(pos)
+        while i < n:
+            j = i + 1
+            while j < n and j - i < bm and slot[j] == slot[i] and pos[j] == pos[j - 1] + 1:
+                j += 1
+            out.append((i, j - i, int(slot[i]), int(pos[i])))
+            i = j
+        return np.array(out, dtype=np.int32).reshape(-1, 4)
+
+    def _forward_rows(self, x, pos, slot, max_len, pos_h=None, slot_h=None):
+        """Packed causal prefill of rows x [n, H] (bf16, consumed) at positions pos into cache rows slot; with the
+        positions and cache rows on the host too, attention runs on query blocks (the tensor-core prefill kernel)."""
         n = x.shape[0]
         assert n <= self.pf_rows
         self.pf_pos[:n].copy_(pos, non_blocking=True)
         self.pf_slot[:n].copy_(slot, non_blocking=True)
+        nb = 0
+        if pos_h is not None:
+            blk = self.query_blocks(pos_h, slot_h)
+            nb = blk.shape[0]
+            assert nb <= self.pf_blocks.shape[0]
+            self.pf_blocks[:nb].copy_(torch.from_numpy(blk))
         run = L.A8StackRun(x=L.ptr(x), ldx=self.H, rows=n, pos=L.ptr(self.pf_pos), slot=L.ptr(self.pf_slot),
                            lens=None, lens_max=0, rowmap=L.ptr(self.pf_slot), max_len=int(max_len),
-                           scratch=self.scratch.desc)
+                           scratch=self.scratch.desc, blocks=L.ptr(self.pf_blocks) if nb else None, nblocks=nb)
         L.call("a8_stack_forward", C.byref(self.slow.desc), C.byref(run), L.stream_handle())
         return self.scratch.h[:n]
 
+    def _embed_rows(self, rows, out):
+        """Prompt rows (host int32, as _prompt_rows) -> their input embeddings in `out` [n, H] (bf16, device)."""
+        n = rows.shape[0]
+        dev_rows = torch.from_numpy(np.ascontiguousarray(rows)).to(self.dev)
+        L.call("a8_embed_prompt", L.ptr(dev_rows), self.ncg, self.cbk, L.ptr(self.emb), L.ptr(self.cbemb),
+               L.ptr(out), self.H, n, self.H, self.emb.shape[0], L.stream_handle())
+        return out[:n]
+
+    def _kv_segments(self, Lp):
+        """A8StateSeg table (device) of a cache row's first Lp positions of every slow layer's K and V: a prefix's K/V
+        as one blob [K / V, kv head, layer, Lp, hd] that a8_state_rows snapshots from the scratch row and loads into
+        slots."""
+        st = self.slow
+        es = 2
+        per_pos = st.hd * es
+        segs, off = [], 0
+        for cache in (st.kc, st.vc):
+            for h in range(st.nkv):
+                segs.append(L.A8StateSeg(base=cache.data_ptr() + h * st.cache_len * per_pos,
+                                         slot_stride=st.nkv * st.cache_len * per_pos, chunk_bytes=Lp * per_pos,
+                                         chunk_stride=st.cache_rows * st.nkv * st.cache_len * per_pos,
+                                         nchunks=st.layers, blob_off=off))
+                off += st.layers * Lp * per_pos
+        raw = bytes((L.A8StateSeg * len(segs))(*segs))
+        return torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(self.dev), len(segs), off
+
     def _prefix_kv(self, pkey, prefix):
-        """A voice prefix's K/V for every slow layer, computed once into the scratch row and kept (:1073-1087)."""
+        """A voice prefix's K/V for every slow layer, computed once into the scratch row and kept as one blob
+        (serve/fast_engine.py:1073-1087); admission loads it into the slots of that voice with one a8_state_rows."""
         hit = self._pkv.get(pkey)
         if hit is not None:
             return hit
         Lp = prefix.shape[0]
-        pos = torch.arange(Lp, dtype=torch.int32, device=self.dev)
-        slot = torch.full((Lp,), self.SCR, dtype=torch.int32, device=self.dev)
         for a in range(0, Lp, self.pf_rows):
             e = min(Lp, a + self.pf_rows)
-            self._forward_rows(prefix[a:e].clone(), pos[a:e], slot[a:e], e)
-        kv = (self.slow.kc[:, self.SCR, :, :Lp].clone(), self.slow.vc[:, self.SCR, :, :Lp].clone())
-        self._pkv[pkey] = kv
-        return kv
+            x = self._embed_rows(prefix[a:e], self.pf_x)
+            pos = torch.arange(a, e, dtype=torch.int32, device=self.dev)
+            slot = torch.full((e - a,), self.SCR, dtype=torch.int32, device=self.dev)
+            self._forward_rows(x, pos, slot, e, np.arange(a, e), np.full(e - a, self.SCR))
+        segs, nseg, nbytes = self._kv_segments(Lp)
+        blob = torch.empty(nbytes, dtype=torch.uint8, device=self.dev)
+        scr = torch.tensor([self.SCR], dtype=torch.int32, device=self.dev)
+        L.call("a8_state_rows", L.ptr(segs), nseg, L.ptr(scr), 1, L.STATE_SNAPSHOT, L.ptr(blob), L.stream_handle())
+        hit = SimpleNamespace(Lp=Lp, blob=blob, segs=segs, nseg=nseg)
+        self._pkv[pkey] = hit
+        return hit
+
+    # ---- packed prefill in a captured graph per token bucket (serve/fast_engine.py:797-853, :1108-1116)
+    def _pf_layout(self):
+        """Offsets (int32 words) of the prefill metadata: ids [NT, 2 + ncg] | pos [NT] | slot [NT] | blocks [NB, 4] |
+        last [NR] | st [NR] | cpos [NR] | frame0 [NR, ncg], NT = the largest token bucket, NB = NT / 64 + NR."""
+        NT, NR = self.pf_NT, self.pf_NR
+        sizes = [NT * (2 + self.ncg), NT, NT, 4 * (NT // 64 + NR), NR, NR, NR, NR * self.ncg]
+        return np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+
+    def _pf_views(self, nt):
+        o, m = self.pf_off, self.pf_meta
+        NR = self.pf_NR
+        v = SimpleNamespace()
+        v.ids = m[o[0]:o[0] + nt * (2 + self.ncg)]
+        v.pos, v.slot = m[o[1]:o[1] + nt], m[o[2]:o[2] + nt]
+        v.nb = nt // 64 + NR
+        v.blocks = m[o[3]:o[3] + 4 * v.nb]
+        v.last, v.st, v.cpos = m[o[4]:o[5]], m[o[5]:o[6]], m[o[6]:o[7]]
+        v.frame0 = m[o[7]:o[8]]
+        return v
+
+    def _pf_body(self, nt):
+        """The prefill of nt packed rows (bucket size) from the static metadata: embeddings, the slow stack with
+        packed causal attention on query blocks, each request's last row, its first token / hidden / position /
+        first codec frame (serve/fast_engine.py:820-835). Padding rows, blocks and requests point at the scratch row;
+        padding blocks are empty."""
+        v = self._pf_views(nt)
+        st = L.stream_handle()
+        L.call("a8_embed_prompt", L.ptr(v.ids), self.ncg, self.cbk, L.ptr(self.emb), L.ptr(self.cbemb),
+               L.ptr(self.pf_x), self.H, nt, self.H, self.emb.shape[0], st)
+        run = L.A8StackRun(x=L.ptr(self.pf_x), ldx=self.H, rows=nt, pos=L.ptr(v.pos), slot=L.ptr(v.slot), lens=None,
+                           lens_max=0, rowmap=L.ptr(v.slot), max_len=self.S, scratch=self.scratch.desc,
+                           blocks=L.ptr(v.blocks), nblocks=v.nb)
+        L.call("a8_stack_forward", C.byref(self.slow.desc), C.byref(run), st)
+        L.call("a8_gather_rows", L.ptr(self.scratch.h), self.H, L.ptr(v.last), L.ptr(self.pf_hl), self.H, self.pf_NR,
+               self.H, st)
+        L.call("a8_prefill_finish", C.byref(self.desc), L.ptr(self.pf_hl), self.pf_NR, L.ptr(v.st), L.ptr(v.cpos),
+               L.ptr(v.frame0), st)
+
+    def _pf_fill(self, nt, slots, parts, starts, frames):
+        """The host metadata of one chunk (padded to bucket nt) into the pinned buffer, then one copy to the device."""
+        h, o = self.pf_meta_h.numpy(), self.pf_off
+        NR, SCR, k = self.pf_NR, self.SCR, len(slots)
+        h[:] = 0
+        ids = h[o[0]:o[0] + nt * (2 + self.ncg)].reshape(nt, 2 + self.ncg)
+        pos, slot = h[o[1]:o[1] + nt], h[o[2]:o[2] + nt]
+        slot[:] = SCR
+        r0 = 0
+        pos_l, slot_l = [], []
+        for s, (_, _, rest), a in zip(slots, parts, starts):
+            n = rest.shape[0]
+            ids[r0:r0 + n] = rest
+            pos[r0:r0 + n] = np.arange(a, a + n)
+            slot[r0:r0 + n] = s
+            r0 += n
+        blk = self.query_blocks(pos[:r0], slot[:r0])
+        nb = nt // 64 + NR
+        assert blk.shape[0] <= nb and k <= NR
+        h[o[3]:o[3] + 4 * blk.shape[0]] = blk.reshape(-1)
+        last, st, cpos = h[o[4]:o[5]], h[o[5]:o[6]], h[o[6]:o[7]]
+        st[:] = SCR
+        ends = np.cumsum([p[2].shape[0] for p in parts]) - 1
+        last[:k] = ends
+        st[:k] = slots
+        cpos[:k] = [a + p[2].shape[0] for a, p in zip(starts, parts)]
+        h[o[7]:o[8]].reshape(NR, self.ncg)[:k] = np.stack([f.cpu().numpy() for f in frames]) if k else 0
+        self.pf_meta[:o[8]].copy_(self.pf_meta_h[:o[8]], non_blocking=True)
+
+    def capture_prefill(self, log=print):
+        """Warm up and record one prefill graph per token bucket (largest first), all padding."""
+        if not self.pf_graph_on:
+            return
+        self._pf_fill(self.pf_NT, [], [], [], [])
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for nt in reversed(self.pf_buckets):
+                for _ in range(2):
+                    self._pf_body(nt)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        for nt in reversed(self.pf_buckets):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._pf_body(nt)
+            self.pf_graphs[nt] = g
+        torch.cuda.synchronize()
 
     @torch.inference_mode()
     def admit(self, slots: List[int], reqs: List[dict]):
@@ -489,14 +651,18 @@ class FastEngine:
         if not reqs:
             return []
         parts = self.build_prompts(reqs)
-        lens = [(p.shape[0] if p is not None else 0) + r.shape[0] for _, p, r in parts]
+        lens = [p.shape[0] + r.shape[0] for _, p, r in parts]
         limit = min(self.S - 32, self.prefill_tokens)
         ok = [i for i, n in enumerate(lens) if n <= limit]
-        cap = min(self.prefill_tokens, self.pf_rows)
+        # chunks a prefill graph takes (tokens <= the largest bucket, requests <= NR); a request whose rest exceeds
+        # the largest bucket goes through pieces of pf_rows rows on its own
         chunk, tot = [], 0
         for i in ok:
             n = parts[i][2].shape[0]
-            if chunk and (tot + n > cap or len(chunk) >= self.B):
+            if n > self.pf_NT:
+                self._prefill_pieces([slots[i]], [reqs[i]], [parts[i]])
+                continue
+            if chunk and (tot + n > self.pf_NT or len(chunk) >= self.pf_NR):
                 self._prefill([slots[k] for k in chunk], [reqs[k] for k in chunk], [parts[k] for k in chunk])
                 chunk, tot = [], 0
             chunk.append(i)
@@ -505,37 +671,78 @@ class FastEngine:
             self._prefill([slots[k] for k in chunk], [reqs[k] for k in chunk], [parts[k] for k in chunk])
         return [n if n <= limit else -1 for n in lens]
 
-    def _prefill(self, slots, reqs, parts):
-        dev = self.dev
-        p0 = {}
-        groups: Dict[str, List[int]] = {}
+    def _load_prefixes(self, slots, parts):
+        """Each voice prefix's cached K/V into its requests' slots (one a8_state_rows per voice); returns the start
+        position of each request's rest."""
+        p0, groups = {}, {}
         for s, (pkey, prefix, _) in zip(slots, parts):
             if pkey is not None:
                 groups.setdefault(pkey, []).append(s)
         for pkey, gslots in groups.items():
             prefix = next(p for (k, p, _) in parts if k == pkey)
-            k, v = self._prefix_kv(pkey, prefix)
-            Lp = prefix.shape[0]
-            idx = torch.tensor(gslots, dtype=torch.long, device=dev)
-            self.slow.kc[:, idx, :, :Lp] = k.unsqueeze(1)
-            self.slow.vc[:, idx, :, :Lp] = v.unsqueeze(1)
+            kv = self._prefix_kv(pkey, prefix)
+            idx = torch.tensor(gslots, dtype=torch.int32).to(self.dev, non_blocking=True)
+            L.call("a8_state_rows", L.ptr(kv.segs), kv.nseg, L.ptr(idx), len(gslots), L.STATE_LOAD, L.ptr(kv.blob),
+                   L.stream_handle())
             for s in gslots:
-                p0[s] = Lp
-        rests = [r for _, _, r in parts]
-        ns = [int(r.shape[0]) for r in rests]
-        starts = [p0.get(s, 0) for s in slots]
-        x = torch.cat(rests, 0).contiguous()
-        pos_h = torch.cat([torch.arange(a, a + n, dtype=torch.int32) for a, n in zip(starts, ns)])
-        pos = pos_h.to(dev)
-        slot_t = torch.cat([torch.full((n,), s, dtype=torch.int32) for n, s in zip(ns, slots)]).to(dev)
+                p0[s] = kv.Lp
+        return [p0.get(s, 0) for s in slots]
+
+    def _codec_rows(self, slots, reqs):
+        """The codec state of admitted rows (serve/fast_engine.py:1134-1156) and the frame each decodes first:
+        keep_voc rows keep their state and decode a silence frame first; the others start clean (silence frame first)
+        or, primed (TTS_VOC_PRIME=1), from their voice's snapshot with its last reference frame."""
+        frames = {}
+        vgroups = {}
+        for s, r in zip(slots, reqs):
+            if r.get("keep_voc"):
+                frames[s] = self.sil_frame
+            else:
+                vgroups.setdefault(r["key"] if self.voc_prime else None, []).append(s)
+        for key, gslots in vgroups.items():
+            snap = self.voc_snaps.get(key) if key is not None else None
+            if snap is None:
+                self.voc.clear_many(gslots)
+                first = self.sil_frame
+            else:
+                self.voc.load_many(gslots, snap[0])
+                first = snap[1].long()
+            for s in gslots:
+                frames[s] = first
+        return [frames[s] for s in slots]
+
+    def _prefill(self, slots, reqs, parts):
+        """One chunk: prefix K/V into the slots, then the packed prefill of the rests in the graph of the smallest
+        token bucket that holds them (eager launches of the same body before capture_prefill)."""
+        starts = self._load_prefixes(slots, parts)
+        frames = self._codec_rows(slots, reqs)
+        n = sum(p[2].shape[0] for p in parts)
+        nt = next(b for b in self.pf_buckets if b >= n)
+        self._pf_fill(nt, slots, parts, starts, frames)
+        g = self.pf_graphs.get(nt)
+        if g is not None:
+            g.replay()
+        else:
+            self._pf_body(nt)
+
+    def _prefill_pieces(self, slots, reqs, parts):
+        """A request whose rest exceeds the largest token bucket: its packed rows in pieces of pf_rows rows (later
+        rows attend to the keys earlier pieces stored), its last row gathered from the piece it ends in."""
+        starts = self._load_prefixes(slots, parts)
+        frames = self._codec_rows(slots, reqs)
+        dev = self.dev
+        rows = np.concatenate([r for _, _, r in parts], 0)
+        ns = [int(r.shape[0]) for _, _, r in parts]
+        pos_h = np.concatenate([np.arange(a, a + n) for a, n in zip(starts, ns)]).astype(np.int32)
+        slot_h = np.concatenate([np.full(n, s) for n, s in zip(ns, slots)]).astype(np.int32)
+        pos, slot_t = torch.from_numpy(pos_h).to(dev), torch.from_numpy(slot_h).to(dev)
         ends = np.cumsum(ns) - 1
-        k, T = len(slots), x.shape[0]
-        # the packed rows in pieces of at most pf_rows: a request may span pieces (its later rows attend to the keys
-        # its earlier rows stored); each request's last row is gathered from the piece it ends in
+        k, T = len(slots), rows.shape[0]
         i0 = 0
         for a in range(0, T, self.pf_rows):
             e = min(T, a + self.pf_rows)
-            h = self._forward_rows(x[a:e], pos[a:e], slot_t[a:e], int(pos_h[a:e].max()) + 1)
+            x = self._embed_rows(rows[a:e], self.pf_x)
+            h = self._forward_rows(x, pos[a:e], slot_t[a:e], int(pos_h[a:e].max()) + 1, pos_h[a:e], slot_h[a:e])
             i1 = i0
             while i1 < k and ends[i1] < e:
                 i1 += 1
@@ -546,26 +753,6 @@ class FastEngine:
             i0 = i1
         self.pf_st[:k].copy_(torch.tensor(slots, dtype=torch.int32))
         self.pf_cpos[:k].copy_(torch.tensor([a + n for a, n in zip(starts, ns)], dtype=torch.int32))
+        fr = torch.stack([f.to(torch.int32).cpu() for f in frames]).to(dev)
         L.call("a8_prefill_finish", C.byref(self.desc), L.ptr(self.pf_hl), k, L.ptr(self.pf_st), L.ptr(self.pf_cpos),
-               L.stream_handle())
-        # codec rows (serve/fast_engine.py:1134-1156): keep_voc rows keep their state and decode a silence frame
-        # first; the others start from their voice's primed snapshot (TTS_VOC_PRIME=1) or clean
-        keep, vgroups = [], {}
-        for s, r in zip(slots, reqs):
-            if r.get("keep_voc"):
-                keep.append(s)
-            else:
-                vgroups.setdefault(r["key"] if self.voc_prime else None, []).append(s)
-        if keep:
-            idx = torch.tensor(keep, dtype=torch.long, device=dev)
-            self.frame_prev.index_copy_(0, idx, self.sil_frame.unsqueeze(0).expand(len(keep), -1).contiguous())
-        for key, gslots in vgroups.items():
-            snap = self.voc_snaps.get(key) if key is not None else None
-            idx = torch.tensor(gslots, dtype=torch.long, device=dev)
-            if snap is None:
-                self.voc.clear_many(gslots)
-                first = self.sil_frame
-            else:
-                self.voc.load_many(gslots, snap[0])
-                first = snap[1].to(dev).long()
-            self.frame_prev.index_copy_(0, idx, first.unsqueeze(0).expand(len(gslots), -1).contiguous())
+               L.ptr(fr), L.stream_handle())

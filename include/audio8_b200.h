@@ -51,7 +51,10 @@ enum {
   A8_EPI_ROPE = 3,      /* fused qkv epilogue: bias, RoPE (rotate_half, fp32, one rounding), q -> y [M, nq, hd],
                            k / v -> caches at [slot, head, pos % ring]                                      */
   A8_EPI_GELU = 4,      /* y bf16: bf16(gelu_erf(bf16(acc + bias)))                                        */
-  A8_EPI_LSRES = 5      /* y bf16: bf16(res + bf16(gamma * bf16(acc + bias)))  (ConvNeXt layer scale)      */
+  A8_EPI_LSRES = 5,     /* y bf16: bf16(res + bf16(gamma * bf16(acc + bias)))  (ConvNeXt layer scale)      */
+  A8_EPI_RESID = 6      /* y bf16: bf16(bf16(acc + bias) + res), the residual add of rmsnorm
+                           (serve/fast_kernels.py:36-40; y may equal res); with ssq_out, each 128-column tile t
+                           also writes ssq_out[t * ssq_ld + m] = sum of y[m, 128 t .. 128 t + 127]^2 (fp32)       */
 };
 
 typedef struct A8Epilogue {
@@ -65,10 +68,20 @@ typedef struct A8Epilogue {
   void* kc;          /* bf16 [rows, nkv, cache_len, hd] */
   void* vc;
   int nq, nkv, hd, ring, cache_len;
-  /* A8_EPI_LSRES */
+  /* A8_EPI_LSRES, A8_EPI_RESID */
   const void* gamma; /* bf16 [N] */
   const void* res;   /* bf16 [M, ldres] (may equal y) */
   int ldres;
+  /* A8_EPI_RESID: per-row sums of squares of y, one partial per 128-column tile (NULL: none) */
+  float* ssq_out;
+  int ssq_ld;        /* row stride of the partials (>= M) */
+  /* Operand normalisation, any kind (NULL norm_w: none): before the MMA reads it, every X row is replaced by
+   * bf16(norm_w * bf16(x * rsqrt(ss / K + eps))), ss = the sum over t < ceil(K / 128) of ssq_in[t * ssq_ld + m]
+   * in t order -- the RMSNorm of serve/fast_kernels.py:41-45 on rows whose sums of squares an A8_EPI_RESID GEMM
+   * wrote. K <= 1024. */
+  const void* norm_w; /* bf16 [K] */
+  const float* ssq_in;
+  float eps;
 } A8Epilogue;
 
 /* y = epilogue(x[M, K] . w[N, K]^T). x row stride ldx, w dense; bf16. Replaces GemmDispatch / linear_triton
@@ -91,6 +104,16 @@ int a8_attention(const void* q, int q_stride, const void* kc, const void* vc, in
                  int nkv, int hd, int cache_len, int layer, const int* lens, const int* rowmap, int rows, int max_len,
                  float scale, void* out, int out_stride, float* ws, long long ws_floats, int* counters, int n_counters,
                  a8_stream_t stream);
+
+/* Packed causal prefill attention on the tensor cores (replaces prefill_attention / PrefillPlan,
+ * serve/fast_kernels.py:296-358): blocks int32 [nblocks][4] = (q0, n, slot, pos0), each up to 64 consecutive packed
+ * rows of one request -- row q0 + r is at position pos0 + r of cache row `slot` and attends keys [0, pos0 + r] of it
+ * (stored beforehand); a block with n = 0 is skipped. q / out bf16 [rows, stride] rows of nq * hd (16-byte aligned
+ * rows), caches as a8_attention; hd 64, nq / nkv <= 8. Softmax with the exact row maximum in two passes over the keys,
+ * P rounded to bf16 for P.V, as the reference's kernel feeds its tl.dot. scale <= 0: hd^-0.5. */
+int a8_prefill_attention(const void* q, int q_stride, const void* kc, const void* vc, int layers, int cache_rows,
+                         int nq, int nkv, int hd, int cache_len, int layer, const int* blocks, int nblocks, int rows,
+                         float scale, void* out, int out_stride, a8_stream_t stream);
 
 /* Size of the library-owned workspace of a8_attention_noalloc, in 4-byte words (5 MiB): the largest need of any valid
  * call (hd 128 at rows * nkv = 295: 590 split parts x 2080 words + 295 tickets = 1,227,495 words). */
@@ -122,6 +145,10 @@ int a8_rmsnorm(const void* x, int ldx, void* res, int ldr, const void* w, void* 
 /* x[r] = emb[sem[r]] + bf16(sum_k cbemb[codes[r, k] + cbk k]) (serve/fast_engine.py:715-717). */
 int a8_embed_frame(const int64_t* sem, const int64_t* codes, int ncb, int cbk, const void* emb, const void* cbemb,
                    void* x, int ldx, int rows, int H, int vocab, a8_stream_t stream);
+/* Packed prompt rows (serve/fast_engine.py:941-945): ids int32 [rows][2 + ncb] = (sem, audio, code_0 ..): x[r] =
+ * emb[sem] on text rows, bf16(emb[sem] + bf16(sum_k cbemb[code_k + cbk k])) on audio rows. */
+int a8_embed_prompt(const int* ids, int ncb, int cbk, const void* emb, const void* cbemb, void* x, int ldx, int rows,
+                    int H, int vocab, a8_stream_t stream);
 /* Tick start (serve/fast_engine.py:742-749, :705): tok_in = tok, codes[:, 0] = clamp(tok - sb), fast AR rows
  * x2[2r] = hid[r], x2[2r+1] = fast_emb[codes[r, 0]]; tick_id[0] = ctr[0]++ (ctr may be NULL). */
 int a8_tick_start(const int64_t* tok, int64_t* tok_in, int64_t* codes, int ncb, long long sb, int cbk, const void* hid,
@@ -205,6 +232,8 @@ typedef struct A8Scratch {
   long long attn_ws_floats;
   int* attn_counters;   /* zeroed once */
   int n_attn_counters;
+  float* ssq;           /* [8, ssq_ld]: per-row sums of squares of the residual stream, one partial per 128 columns */
+  int ssq_ld;           /* rows the partials hold (>= the rows of any call) */
 } A8Scratch;
 
 /* A transformer stack on packed weights (serve/fast_engine.py:82-115): q / k rows of wqkv permuted per head for
@@ -239,6 +268,9 @@ typedef struct A8StackRun {
   const int* rowmap;    /* int32 [rows] cache row attended (NULL: the row index) */
   int max_len;          /* bound of any row's keys (0: cache_len); sets the split count */
   A8Scratch scratch;    /* output in scratch.h */
+  const int* blocks;    /* packed causal prefill (hd 64): int32 [nblocks][4] query blocks as a8_prefill_attention
+                           (pos / slot must agree); NULL: every row by the decode attention */
+  int nblocks;
 } A8StackRun;
 
 /* _Stack.forward (serve/fast_engine.py:117-138): decode rows or packed causal prefill rows. */
@@ -418,9 +450,11 @@ int a8_slow_step(const A8Engine* e, int b, a8_stream_t stream);
 
 /* Admission tail for n requests (serve/fast_engine.py:1124-1133 and _pf_body :828-835): h_last bf16 [n, H] = each
  * request's final-normed last prompt row; first token drawn without the RAS window (noise stream 18 at the current
- * tick count), written with hid, cpos = cpos_new into slots[i]; prev and nstep of those slots cleared. */
+ * tick count), written with hid, cpos = cpos_new into slots[i]; prev and nstep of those slots cleared; with frame0
+ * (int32 [n, ncb], or NULL) frame_prev[slots[i]] = frame0[i], the frame the slot's codec decodes first (:1138-1156).
+ * A request aimed at slot B or beyond (a prefill graph's padding) draws and writes nothing. */
 int a8_prefill_finish(const A8Engine* e, const void* h_last, int n, const int* slots, const int* cpos_new,
-                      a8_stream_t stream);
+                      const int* frame0, a8_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -280,9 +280,10 @@ class Stack:
         self.kc = torch.zeros(len(self.layers), cache_rows, nkv, cache_len, hd)
         self.vc = torch.zeros_like(self.kc)
 
-    def forward(self, x, pos, slot, lens=None, rowmap=True, blocks=None):
+    def forward(self, x, pos, slot, lens=None, rowmap=True, blocks=None, trace=None):
         """x: [R, H] bf16-valued. Decode (blocks None): row r attends [0, lens[r]) of cache row slot[r] (rowmap) or
-        row r. Prefill: `blocks` as in prefill_attention. Returns the final-normed hidden [R, H]."""
+        row r. Prefill: `blocks` as in prefill_attention. Returns the final-normed hidden [R, H]. trace (tests): a
+        list that receives the residual stream after every layer."""
         R = x.shape[0]
         nl = len(self.layers)
         h = rmsnorm(x, self.layers[0].ln1, self.eps)
@@ -300,6 +301,8 @@ class Stack:
             m = linear(silu_mul(linear(h, L.w13)), L.w2)
             nxt = self.layers[i + 1].ln1 if i + 1 < nl else self.norm
             h, res = rmsnorm(m, nxt, self.eps, residual=res)
+            if trace is not None:
+                trace.append(res.clone())
         return h
 
 

@@ -18,6 +18,7 @@ def test_null_pointers_rejected(lib):
     N = None
     assert lib.a8_gemm(N, 896, N, 896, 896, 4, N, 896, N, 0, N) == ARG
     assert lib.a8_attention(N, 896, N, N, 1, 1, 14, 2, 64, 64, 0, N, N, 1, 64, 0.0, N, 896, N, 0, N, 0, N) == ARG
+    assert lib.a8_prefill_attention(N, 896, N, N, 1, 1, 14, 2, 64, 64, 0, N, 1, 1, 0.0, N, 896, N) == ARG
     assert lib.a8_rmsnorm(N, 896, N, 0, N, N, 896, 4, 896, 1e-6, N) == ARG
     assert lib.a8_embed_frame(N, N, 10, 4096, N, N, N, 896, 4, 896, 151680, N) == ARG
     assert lib.a8_gather_rows(N, 896, N, N, 896, 4, 896, N) == ARG
@@ -33,7 +34,7 @@ def test_null_pointers_rejected(lib):
     assert lib.a8_stack_forward(N, N, N) == ARG
     assert lib.a8_tick(N, 1, N) == ARG
     assert lib.a8_slow_step(N, 1, N) == ARG
-    assert lib.a8_prefill_finish(N, N, 1, N, N, N) == ARG
+    assert lib.a8_prefill_finish(N, N, 1, N, N, N, N) == ARG
     assert lib.a8_resample_reset(N, N, N, 1, 1, N) == ARG
     assert lib.a8_resample_step(N, N, 2048, N, 0, 1, N, N, 832, N, N) == ARG
 
@@ -122,3 +123,15 @@ def test_noalloc_rejects_before_touching_its_array(lib):
     assert lib.a8_attention_noalloc(p, 896, p, p, 1, 1, 14, 2, 96, 64, 0, p, N, 1, 64, 0.0, p, 896, N) == ARG  # hd
     assert lib.a8_attention_noalloc(p, 896, p, p, 1, 1, 14, 2, 64, 64, 1, p, N, 1, 64, 0.0, p, 896, N) == ARG  # layer
     assert lib.a8_attention_noalloc(p, 896, p, p, 1, 1, 14, 2, 64, 64, 0, p, N, 1, 65, 0.0, p, 896, N) == ARG  # len
+
+
+def test_prefill_attention_shape_checks(lib):
+    """The tensor-core prefill attention takes hd 64 and groups of at most 8 query heads; rows need 16-byte alignment
+    (they are TMA tiles); all checked before any device work."""
+    p, N = C.c_void_p(256), None
+    assert lib.a8_prefill_attention(p, 1024, p, p, 1, 1, 8, 8, 128, 64, 0, p, 1, 1, 0.0, p, 1024, N) == ARG   # hd
+    assert lib.a8_prefill_attention(p, 896, p, p, 1, 1, 14, 1, 64, 64, 0, p, 1, 1, 0.0, p, 896, N) == ARG   # group 14
+    assert lib.a8_prefill_attention(p, 896, p, p, 1, 1, 14, 2, 64, 64, 0, p, 0, 1, 0.0, p, 896, N) == ARG   # no blocks
+    assert lib.a8_prefill_attention(p, 900, p, p, 1, 1, 14, 2, 64, 64, 0, p, 1, 1, 0.0, p, 896, N) == 3     # stride
+    assert lib.a8_prefill_attention(C.c_void_p(258), 896, p, p, 1, 1, 14, 2, 64, 64, 0, p, 1, 1, 0.0, p, 896,
+                                    N) == 3                                                                 # q align

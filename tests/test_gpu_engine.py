@@ -260,3 +260,42 @@ def test_engine_tick_audio_is_codec_of_previous_frame(a8, dev, tiny_model):
         torch.cuda.synchronize()
         assert torch.equal(eng.audio[:3], want), t
     assert a8.device_error()[0] == 0
+
+
+def test_admission_graph_equals_eager_and_launches_only_library_kernels(a8, dev, tiny_model):
+    """An admission chunk is one metadata copy and one replay of the prefill graph of its token bucket: the state it
+    leaves (first tokens, hidden, positions, K/V, first codec frames) is bit-identical to the same launches made
+    eagerly, and every kernel it runs is this library's (the prompt embedding, the prefix K/V copy and the codec
+    state included: no PyTorch kernel)."""
+    gp = dict(do_sample=True, temperature=0.8, top_k=50, top_p=0.95)
+    mk = lambda: a8.FastEngine(tiny_model, StubTokenizer(), gp, max_slots=4, max_seq=512, buckets=[4],
+                               seq_from_env=False, seed=21)
+    eager, graphed = mk(), mk()
+    graphed.capture(log=lambda *a: None)
+    assert sorted(graphed.pf_graphs) == graphed.pf_buckets
+    reqs = _requests(4) + [dict(_requests(5)[0], key="v1")]
+    for eng in (eager, graphed):                 # a first admission caches the voices' prefix K/V
+        eng.admit([0, 1, 2], reqs)
+    torch.cuda.synchronize()
+    names = None
+    try:
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            graphed.admit([3, 1], [reqs[1], reqs[2]])
+            torch.cuda.synchronize()
+        names = {e.name for e in prof.events() if str(e.device_type).endswith("CUDA")}
+    except Exception as exc:                      # no CUPTI on this box: the equality checks below still run
+        print("profiler unavailable:", exc)
+    eager.admit([3, 1], [reqs[1], reqs[2]])
+    torch.cuda.synchronize()
+    assert a8.device_error()[0] == 0
+    for name in ("tok", "hid", "cpos", "prev", "nstep", "frame_prev"):
+        assert torch.equal(getattr(eager, name), getattr(graphed, name)), name
+    for s in (0, 1, 2, 3):                        # what admission wrote: each slot's first cpos positions
+        n = int(eager.cpos[s])
+        assert torch.equal(eager.slow.kc[:, s, :, :n], graphed.slow.kc[:, s, :, :n]), s
+        assert torch.equal(eager.slow.vc[:, s, :, :n], graphed.slow.vc[:, s, :, :n]), s
+    if names:
+        kernels = {n for n in names if not n.lower().startswith("memcpy") and not n.lower().startswith("memset")}
+        print("admission kernels:", sorted(kernels))
+        assert kernels and all(n.startswith("a8::") or "a8::" in n for n in kernels), sorted(kernels)

@@ -99,6 +99,73 @@ def test_gemm_bias_gelu_lsres_f32(L, ws):
     assert bool((lg[:, N2:] == 7.0).all())                       # nothing written past N
 
 
+@pytest.mark.parametrize("M,D,splits", [(1, 896, 0), (64, 896, 0), (192, 896, 0), (223, 1024, 0), (384, 896, 3),
+                                         (1000, 896, 0), (2048, 1024, 0)])
+def test_gemm_resid_then_normed_operand(L, ws, M, D, splits):
+    """The fused RMSNorm of the stacks: an A8_EPI_RESID GEMM adds its output to the residual stream in place and
+    writes per-row sums of squares per 128 columns; the next GEMM normalises that stream in its operand producer.
+    Against the oracle's linear + rmsnorm(residual) + linear (serve/fast_kernels.py:30-46)."""
+    from audio8_b200.engine import interleave_w13
+    g = torch.Generator().manual_seed(M + D)
+    K1, I, eps = 896, 1024, 1e-6
+    x, w = rnd(g, M, K1), rnd(g, D, K1, scale=K1 ** -0.5)
+    res = rnd(g, M, D)
+    lnw = (1.0 + 0.1 * torch.randn(D, generator=g)).to(BF)
+    w1, w3 = rnd(g, I, D, scale=D ** -0.5), rnd(g, I, D, scale=D ** -0.5)
+    # oracle
+    a_o = R.linear(x.float(), w.float())
+    h_o, r_o = R.rmsnorm(a_o, lnw.float(), eps, residual=res.float())
+    y_o = R.silu_mul(torch.cat([R.linear(h_o, w1.float()), R.linear(h_o, w3.float())], -1))
+    # device: residual add + partial sums of squares, then the normalised operand of the SiLU GEMM
+    RS = res.cuda().contiguous()
+    ssq = torch.full((8, M + 5), float("nan"), device="cuda")
+    e1 = L.A8Epilogue(kind=L.EPI_RESID, res=L.ptr(RS), ldres=D, ssq_out=L.ptr(ssq), ssq_ld=M + 5)
+    gemm(L, ws, x.cuda(), w.cuda(), RS, e1, splits)
+    assert rel(RS, r_o) < 1e-2 and frac_equal(RS, r_o) > 0.97
+    t = -(-D // 128)
+    ss_ref = (RS.float().cpu() ** 2).view(M, t, 128).sum(-1).t()
+    assert torch.allclose(ssq[:t, :M].cpu(), ss_ref, rtol=1e-5, atol=1e-5)
+    LN = lnw.cuda()
+    e2 = L.A8Epilogue(kind=L.EPI_SILU, norm_w=L.ptr(LN), ssq_in=L.ptr(ssq), ssq_ld=M + 5, eps=eps)
+    y = torch.zeros(M, I, dtype=BF, device="cuda")
+    gemm(L, ws, RS, interleave_w13(w1, w3).cuda(), y, e2, ldy=I)
+    # the engine's own residual (bit-level differences in RS propagate), so compare against the oracle norm of RS
+    h_e = R.rmsnorm(RS.float().cpu(), lnw.float(), eps)
+    y_e = R.silu_mul(torch.cat([R.linear(h_e, w1.float()), R.linear(h_e, w3.float())], -1))
+    assert rel(y, y_e) < 1e-2 and frac_equal(y, y_e) > 0.97, (rel(y, y_e), frac_equal(y, y_e))
+    assert rel(y, y_o) < 2e-2
+
+
+@pytest.mark.parametrize("layout", ["mixed", "long"])
+def test_prefill_attention_blocks(L, layout):
+    """a8_prefill_attention (tcgen05, query blocks of up to 64 rows) against the oracle's packed causal attention
+    (serve/fast_kernels.py:296-332): requests continuing after a prefix already in their cache row, blocks shorter
+    than 64 rows, a one-row request, a padding block (n = 0), GQA 14 / 2 at hd 64, layer 1 of 2."""
+    g = torch.Generator().manual_seed(3 if layout == "mixed" else 4)
+    nq, nkv, hd, S, layers, rows_c = 14, 2, 64, 2048, 2, 5
+    reqs = [(1, 0, 70), (3, 150, 20), (0, 64, 133), (2, 500, 1), (4, 7, 64)] if layout == "mixed" else \
+        [(2, 1900, 140), (0, 0, 300)]
+    R_ = sum(n for _, _, n in reqs)
+    q = rnd(g, R_, nq * hd)
+    kc, vc = rnd(g, layers, rows_c, nkv, S, hd), rnd(g, layers, rows_c, nkv, S, hd)
+    blocks, r0 = [], 0
+    for slot, p0, n in reqs:
+        blocks += [(r0 + a, min(64, n - a), slot, p0 + a) for a in range(0, n, 64)]
+        r0 += n
+    table = torch.tensor(blocks + [(0, 0, 0, 0)], dtype=torch.int32)
+    ref = R.prefill_attention(q.float().view(R_, nq, hd), kc[1].float(), vc[1].float(), blocks)
+    Q, KC, VC, T = q.cuda(), kc.cuda(), vc.cuda(), table.cuda()
+    out = torch.full((R_, nq * hd), float("nan"), dtype=BF, device="cuda")
+    L.call("a8_prefill_attention", L.ptr(Q), nq * hd, L.ptr(KC), L.ptr(VC), layers, rows_c, nq, nkv, hd, S, 1,
+           L.ptr(T), T.shape[0], R_, 0.0, L.ptr(out), nq * hd, L.stream_handle())
+    torch.cuda.synchronize()
+    assert L.device_error()[0] == 0, L.device_error()
+    assert not torch.isnan(out.float()).any()
+    e = rel(out.view(R_, nq, hd), ref)
+    assert e < 1e-2, e
+    assert frac_equal(out.view(R_, nq, hd), ref) > 0.9
+
+
 @pytest.mark.parametrize("M", [1, 64, 200, 223, 450])
 def test_gemm_silu(L, ws, M):
     from audio8_b200.engine import interleave_w13
