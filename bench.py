@@ -762,6 +762,8 @@ def run_profile(args):
     what = args.profile
     if what == "resample":
         return profile_resample()
+    if what == "admit":
+        return profile_admit()
     a8, eng, step = cfg2_engine()
     L = a8._lib
     if what == "tick":
@@ -782,6 +784,36 @@ def run_profile(args):
     err = a8.device_error()
     assert err[0] == 0, err
     print(json.dumps({"profile": what, "ok": True}), flush=True)
+
+
+def profile_admit(n=8):
+    """One admission chunk of n config-0 requests (100-frame voice prefix, 64 text ids) into an engine of the full
+    stand-in, its voice's prefix K/V cached by a first admission: the packed prefill's kernels (prompt embedding, the
+    24 layers with the tensor-core causal attention, head and first-token draw) between cudaProfilerStart/Stop."""
+    from types import SimpleNamespace
+
+    import torch
+
+    import __graft_entry__ as G
+    from oracle.standin import StandinConfig, StubTokenizer, build_standin
+    G.build()
+    a8 = G.load_package()
+    model = build_standin(0, StandinConfig())
+    eng = a8.FastEngine(model, StubTokenizer(), dict(do_sample=True, temperature=0.8, top_k=50, top_p=0.95),
+                        max_slots=2 * n, max_seq=2048, buckets=[n], seq_from_env=False, seed=5)
+    g = torch.Generator().manual_seed(0)
+    item = SimpleNamespace(ref_code=torch.randint(0, 4096, (100, 10), generator=g), ref_text="12 34 56 78 90")
+    reqs = [dict(text=" ".join(str(int(x)) for x in torch.randint(0, 151643, (64,), generator=g)), item=item,
+                 key="v0") for _ in range(n)]
+    eng.admit(list(range(n)), reqs)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    eng.admit(list(range(n, 2 * n)), reqs)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    err = a8.device_error()
+    assert err[0] == 0, err
+    print(json.dumps({"profile": "admit", "ok": True, "rows": int(eng.cpos[n])}), flush=True)
 
 
 def profile_resample(b=B_CFG2, ticks=20):
@@ -842,9 +874,10 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=None, help="CPU baseline sample: steps (cfg1 3, cfg2 6)")
     ap.add_argument("--cpu-rows", type=int, default=64, help="cfg2 CPU baseline sample: rows of the 192")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--profile", default=None, metavar="tick|conv:I|resample",
+    ap.add_argument("--profile", default=None, metavar="tick|conv:I|resample|admit",
                     help="no timing: run one eager cfg2 tick (or decoder conv I alone at 192 rows, or the 44.1 -> "
-                         "16 kHz resampler step at 192 rows) between cudaProfilerStart/Stop, for ncu "
+                         "16 kHz resampler step at 192 rows, or one admission of 8 config-0 prompts) between "
+                         "cudaProfilerStart/Stop, for ncu "
                          "--profile-from-start off")
     ap.add_argument("--serve-streams", type=int, default=1120,
                     help="cfg2: closed-loop streams a GPU of the serving run reported under `serving`")
