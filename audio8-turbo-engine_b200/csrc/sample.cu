@@ -6,8 +6,9 @@
 //   softmax(v / temperature), exponential race argmax(p_i / E_i), E_i ~ Exp(1).
 // E_i = -log(u_i) with u_i from Philox4x32-10 keyed by the engine seed and counted by (i / 4, row, tick, stream),
 // word i % 4, u = ((w >> 8) + 0.5) * 2^-24 -- so a CPU restatement reproduces every draw bit for bit.
-// Top-k: a 4-pass radix select (8 bits a pass) on order-preserving keys finds the k-th largest value; the candidates
-// are compacted in index order and sorted by a bitonic network on (value desc, index asc).
+// Top-k: a radix select (8 bits a pass; two passes when every logit is a bf16 value, else four) on order-preserving
+// keys finds the k-th largest value; the candidates are compacted in index order and sorted by a bitonic network on
+// (value desc, index asc) -- by one warp for up to 64 of them -- and for k <= 64 each race is one warp's.
 #include "common.cuh"
 
 namespace a8 {
@@ -176,6 +177,75 @@ __device__ int race(const float* s_v, const float* s_cum, int k, float p, float 
   return bi;
 }
 
+// The same draw by one warp, for k <= 64 (two candidates a lane, warp shuffles only). The softmax normaliser is a
+// common factor of every score, so the winner does not depend on the order of its sum.
+__device__ int race_warp(const float* s_v, const float* s_cum, int k, float p, float t, unsigned long long seed,
+                         int stream, long long tick, int row) {
+  const int lane = threadIdx.x & 31;
+  const float z0 = s_v[0] / t;
+  float e[2];
+  float part = 0.f;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int i = lane + 32 * h;
+    const bool keep = i < k && ((i == 0) || !(p < 1.0f && s_cum[i] > p));
+    e[h] = keep ? expf(s_v[i] / t - z0) : 0.f;
+    part += e[h];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffff, part, o);
+  float best = -INFINITY;
+  int bi = 0x7FFFFFFF;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int i = lane + 32 * h;
+    if (i < k) {
+      const float sc = (e[h] / part) / exp_noise(seed, stream, tick, row, i);
+      if (sc > best || (sc == best && i < bi)) { best = sc; bi = i; }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffff, best, o);
+    const int oi = __shfl_xor_sync(0xffffffff, bi, o);
+    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+  }
+  return bi;
+}
+
+// Descending bitonic sort of s_c[0, 64) by one warp (two entries a lane), 64-bit keys.
+__device__ void sort64_warp(unsigned long long* s_c) {
+  const int lane = threadIdx.x & 31;
+  unsigned long long x[2] = {s_c[2 * lane], s_c[2 * lane + 1]};
+#pragma unroll
+  for (int size = 2; size <= 64; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int pidx = 2 * lane + h;
+        const bool desc = (pidx & size) == 0;
+        unsigned long long y;
+        if (stride == 1) {
+          y = x[h ^ 1];
+        } else {
+          y = __shfl_xor_sync(0xffffffff, x[h], stride >> 1);
+        }
+        const bool lower = (pidx & stride) == 0;         // this entry is the lower index of its pair
+        const bool keep_max = desc == lower;
+        if (stride != 1) x[h] = keep_max ? (x[h] > y ? x[h] : y) : (x[h] < y ? x[h] : y);
+        else if (h == 0) {                               // both entries of the pair live in this lane
+          const unsigned long long hi = x[0] > x[1] ? x[0] : x[1], lo = x[0] > x[1] ? x[1] : x[0];
+          x[0] = keep_max ? hi : lo;
+          x[1] = keep_max ? lo : hi;
+        }
+      }
+    }
+  }
+  s_c[2 * lane] = x[0];
+  s_c[2 * lane + 1] = x[1];
+}
+
 __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const SampleArgs a) {
   extern __shared__ uint8_t smem_raw[];
   float* s_x = reinterpret_cast<float*>(smem_raw);                       // [V]
@@ -186,7 +256,7 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const SampleArgs a) {
   int kp2 = 1;
   while (kp2 < a.k) kp2 <<= 1;
   unsigned long long* s_c = reinterpret_cast<unsigned long long*>(
-      (reinterpret_cast<uintptr_t>(s_idx + ((a.k + 3) & ~3)) + 7) & ~uintptr_t(7));   // [kp2]
+      (reinterpret_cast<uintptr_t>(s_idx + ((a.k + 3) & ~3)) + 7) & ~uintptr_t(7));   // [max(kp2, 64)]
   __shared__ float red[32];
   __shared__ int redi[32];
   __shared__ int hist[256];
@@ -213,17 +283,23 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const SampleArgs a) {
     j1 = bi;
   } else {
     const int k = a.k;
-    // log-sum-exp of all logits
+    // log-sum-exp of all logits; whether every logit is a bf16 value (its low 16 bits zero: the head GEMM's logits)
     float mx = -INFINITY;
-    for (int i = tid; i < V; i += SAMPLE_THREADS) mx = fmaxf(mx, s_x[i]);
+    uint32_t low = 0;
+    for (int i = tid; i < V; i += SAMPLE_THREADS) {
+      mx = fmaxf(mx, s_x[i]);
+      low |= __float_as_uint(s_x[i]) & 0xFFFFu;
+    }
+    const bool bf16_keys = !__syncthreads_or(low != 0u);
     mx = block_max(mx, red);
     float se = 0.f;
     for (int i = tid; i < V; i += SAMPLE_THREADS) se += expf(s_x[i] - mx);
     const float lse = mx + logf(block_sum(se, red));
-    // radix select of the k-th largest key
+    // radix select of the k-th largest key (bf16 values: the high 16 bits of a key decide, two passes)
     uint32_t prefix = 0, mask = 0;
     int remain = k;
-    for (int shift = 24; shift >= 0; shift -= 8) {
+    const int last_shift = bf16_keys ? 16 : 0;
+    for (int shift = 24; shift >= last_shift; shift -= 8) {
       for (int b = tid; b < 256; b += SAMPLE_THREADS) hist[b] = 0;
       __syncthreads();
       // logits crowd into few bins of the high bytes: lanes of a warp with the same bin add once, together
@@ -268,7 +344,9 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const SampleArgs a) {
       remain -= s_sel[1];
       __syncthreads();
     }
-    const uint32_t T = prefix;             // key of the k-th largest; take `remain` of the ties, lowest index first
+    // key of the k-th largest; take `remain` of the ties, lowest index first. With bf16 values the low half of a key
+    // follows from its sign: 0 for a positive value, 0xFFFF for a negative one (the key of a negative value is ~u)
+    const uint32_t T = bf16_keys ? (prefix | ((prefix & 0x80000000u) ? 0u : 0xFFFFu)) : prefix;
     // compaction in index order: thread owns a contiguous index range
     const int per = (V + SAMPLE_THREADS - 1) / SAMPLE_THREADS;
     const int i0 = tid * per, i1 = min(V, i0 + per);
@@ -296,8 +374,17 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const SampleArgs a) {
       }
     }
     __syncthreads();
-    // bitonic sort, descending
-    for (int size = 2; size <= kp2; size <<= 1) {
+    // bitonic sort, descending (one warp for up to 64 candidates)
+    if (kp2 <= 64) {
+      if (tid < 32) {
+        if (kp2 < 64)
+          for (int i = kp2 + tid; i < 64; i += 32) s_c[i] = 0ull;
+        __syncwarp();
+        sort64_warp(s_c);
+      }
+      __syncthreads();
+    }
+    for (int size = 2; size <= kp2 && kp2 > 64; size <<= 1) {
       for (int stride = size >> 1; stride > 0; stride >>= 1) {
         for (int i = tid; i < kp2; i += SAMPLE_THREADS) {
           const int jx = i ^ stride;
@@ -331,11 +418,26 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const SampleArgs a) {
       }
     }
     __syncthreads();
-    const int c1 = race(s_v, s_cum, k, a.p, a.t, a.seed, a.stream1, tick, row, red, redi);
-    j1 = s_idx[c1];
-    if (a.mode == SM_SEMANTIC) {
-      const int c2 = race(s_v, s_cum, k, a.p2, a.t2, a.seed, a.stream2, tick, row, red, redi);
-      j2 = s_idx[c2];
+    if (k <= 64) {
+      // the regular draw by warp 0, the RAS redraw by warp 1, side by side
+      __shared__ int s_pick[2];
+      if (tid < 32) {
+        const int c1 = race_warp(s_v, s_cum, k, a.p, a.t, a.seed, a.stream1, tick, row);
+        if (tid == 0) s_pick[0] = c1;
+      } else if (tid < 64 && a.mode == SM_SEMANTIC) {
+        const int c2 = race_warp(s_v, s_cum, k, a.p2, a.t2, a.seed, a.stream2, tick, row);
+        if (tid == 32) s_pick[1] = c2;
+      }
+      __syncthreads();
+      j1 = s_idx[s_pick[0]];
+      if (a.mode == SM_SEMANTIC) j2 = s_idx[s_pick[1]];
+    } else {
+      const int c1 = race(s_v, s_cum, k, a.p, a.t, a.seed, a.stream1, tick, row, red, redi);
+      j1 = s_idx[c1];
+      if (a.mode == SM_SEMANTIC) {
+        const int c2 = race(s_v, s_cum, k, a.p2, a.t2, a.seed, a.stream2, tick, row, red, redi);
+        j2 = s_idx[c2];
+      }
     }
   }
 
@@ -397,6 +499,7 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(const SampleArgs a) {
 int sample_smem(int V, int k) {
   int kp2 = 1;
   while (kp2 < k) kp2 <<= 1;
+  if (kp2 < 64) kp2 = 64;                  // the one-warp sort pads the candidates to 64
   return ((V + 3) & ~3) * 4 + 3 * ((k + 3) & ~3) * 4 + 8 + kp2 * 8;
 }
 

@@ -764,6 +764,8 @@ def run_profile(args):
         return profile_resample()
     if what == "admit":
         return profile_admit()
+    if what == "sample":
+        return profile_sample()
     a8, eng, step = cfg2_engine()
     L = a8._lib
     if what == "tick":
@@ -814,6 +816,35 @@ def profile_admit(n=8):
     err = a8.device_error()
     assert err[0] == 0, err
     print(json.dumps({"profile": "admit", "ok": True, "rows": int(eng.cpos[n])}), flush=True)
+
+
+def profile_sample(rows=B_CFG2, V=4097, launches=4):
+    """`launches` sampled draws (top-k 50, top-p 0.95, temperature 0.8) over rows x V logits rounded to bf16, as the
+    semantic head gives them (capture the last with `ncu -s launches-1 -c 1`), then 20 timed with CUDA events."""
+    import torch
+
+    import __graft_entry__ as G
+    G.build()
+    a8 = G.load_package()
+    L = a8._lib
+    g = torch.Generator().manual_seed(0)
+    lg = (torch.randn(rows, V + 3, generator=g) * 3).to(torch.bfloat16).float().cuda()
+    out = torch.empty(rows, dtype=torch.int64, device="cuda")
+    call = lambda: L.call("a8_sample", L.ptr(lg), V + 3, V, rows, 1, 50, 0.95, 0.8, 7, 16, None, L.ptr(out),
+                          L.stream_handle())
+    for _ in range(launches):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(20):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    err = a8.device_error()
+    assert err[0] == 0, err
+    print(json.dumps({"profile": "sample", "rows": rows, "V": V, "us_per_launch": round(e0.elapsed_time(e1) * 50, 2)}),
+          flush=True)
 
 
 def profile_resample(b=B_CFG2, ticks=20):
@@ -874,9 +905,10 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=None, help="CPU baseline sample: steps (cfg1 3, cfg2 6)")
     ap.add_argument("--cpu-rows", type=int, default=64, help="cfg2 CPU baseline sample: rows of the 192")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--profile", default=None, metavar="tick|conv:I|resample|admit",
+    ap.add_argument("--profile", default=None, metavar="tick|conv:I|resample|admit|sample",
                     help="no timing: run one eager cfg2 tick (or decoder conv I alone at 192 rows, or the 44.1 -> "
-                         "16 kHz resampler step at 192 rows, or one admission of 8 config-0 prompts) between "
+                         "16 kHz resampler step at 192 rows, one admission of 8 config-0 prompts, or sampler draws over "
+                         "192 x 4097 logits) between "
                          "cudaProfilerStart/Stop, for ncu "
                          "--profile-from-start off")
     ap.add_argument("--serve-streams", type=int, default=1120,
