@@ -81,10 +81,13 @@ __device__ __forceinline__ uint64_t umma_desc_sw64_row(uint32_t addr) {
   return ((uint64_t)((addr >> 4) & 0x3FFFu)) | (1ull << 16) | (32ull << 32) | (1ull << 46) | (4ull << 61);
 }
 
-// sin^2(t) for |t| < 2^15 without branches: t = k pi/2 + r with k = rint(2t/pi) (round-to-nearest by adding 1.5 2^23)
+// sin^2(t) for |t| < 2^21 without branches: t = k pi/2 + r with k = rint(2t/pi) (round-to-nearest by adding 1.5 2^23)
 // and r = t - k pi/2 by a two-term split of pi/2 (Cody-Waite reduction with fused multiply-adds); then
-// sin^2(r) = r^2 P(r^2) with P the Taylor series of (sin r / r)^2 = sum_n (-1)^n 2^(2n+1) r^(2n) / (2n+2)!, which for
-// |r| <= pi/4 is within 1e-10 after seven terms; odd k swaps sin^2 for cos^2 = 1 - sin^2.
+// sin^2(r) = r^2 P(r^2) with P the Taylor series of (sin r / r)^2 = sum_n (-1)^n 2^(2n+1) r^(2n) / (2n+2)!, whose
+// seventh term is below 4e-9 for |r| <= pi/4, so six are kept; odd k swaps sin^2 for cos^2 = 1 - sin^2. Emulated in
+// fp32 with fused multiply-adds against a float64 sin^2 over 2e6 random t a range, the result stays within 1.2e-7
+// absolute for every |t| < 2^22 (the split's error grows as k 2^-48); the epilogue keeps it to |t| < 2^21.
+constexpr float SIN2_RANGE = 2097152.f;
 __device__ __forceinline__ float sin2_reduced(float t) {
   const float big = fmaf(t, 0.636619772367581343f, 12582912.0f);
   const float k = big - 12582912.0f;
@@ -92,8 +95,7 @@ __device__ __forceinline__ float sin2_reduced(float t) {
   float r = fmaf(-k, 1.57079637050628662109375f, t);     // pi/2 rounded to fp32
   r = fmaf(-k, -4.37113900018624283e-8f, r);             // pi/2 minus that
   const float u = r * r;
-  float p = 9.39683970e-8f;                              // 2^13 / 14!
-  p = fmaf(p, u, -4.27556185e-6f);                       // -2^11 / 12!
+  float p = -4.27556185e-6f;                             // -2^11 / 12!
   p = fmaf(p, u, 1.41093474e-4f);                        // 2^9 / 10!
   p = fmaf(p, u, -3.17460317e-3f);                       // -2^7 / 8!
   p = fmaf(p, u, 4.44444444e-2f);                        // 2^5 / 6!
@@ -103,27 +105,38 @@ __device__ __forceinline__ float sin2_reduced(float t) {
   return odd ? 1.0f - s2 : s2;
 }
 
-// The epilogue of one 16-column chunk with the exact conversions and sinf, from the raw accumulators v: fp16 y into
-// hy and, with an activation, fp16 act(y) into ha (two values a word).
-__device__ __forceinline__ void exact_chunk(const ConvArgs& a, const float* v, int b, int t, int nb, bool act,
-                                            uint32_t* hy, uint32_t* ha) {
+// The next conv's input of 16 consecutive outputs: ha = fp16(y + inv sin^2(alpha y)) from the fp16-rounded y (as
+// fp32 in v) and the channels' alpha / inv staged in shared memory (16-byte aligned), two values a word. CHECK: also
+// report whether every |alpha y| stayed inside sin2_reduced's range.
+template <bool CHECK>
+__device__ __forceinline__ bool snake16(const float* v, const float* al_s, const float* iv_s, uint32_t* ha) {
+  bool ok = true;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int n = nb + i;
-    float x = v[i];
-    if (a.bias != nullptr) x += a.bias[n];
-    if (a.res != nullptr) x += __half2float(a.res[(size_t)b * a.res_bs + (size_t)t * a.res_ts + n]);
-    const __half h = __float2half_rn(x);
-    const float y = __half2float(h);
-    const uint32_t hb = __half_as_ushort(h);
-    hy[i / 2] = (i & 1) ? (hy[i / 2] & 0xFFFFu) | (hb << 16) : hb;
-    if (act) {
-      const int c = n % a.cout;
-      const float s = sinf(y * a.alpha[c]);
-      const uint32_t hz = __half_as_ushort(__float2half_rn(y + a.inv[c] * s * s));
-      ha[i / 2] = (i & 1) ? (ha[i / 2] & 0xFFFFu) | (hz << 16) : hz;
-    }
+  for (int i = 0; i < 16; i += 4) {
+    const float4 al = *reinterpret_cast<const float4*>(al_s + i);
+    const float4 iv = *reinterpret_cast<const float4*>(iv_s + i);
+    const float t0 = v[i] * al.x, t1 = v[i + 1] * al.y, t2 = v[i + 2] * al.z, t3 = v[i + 3] * al.w;
+    if (CHECK) ok &= fmaxf(fmaxf(fabsf(t0), fabsf(t1)), fmaxf(fabsf(t2), fabsf(t3))) < SIN2_RANGE;
+    ha[i / 2] = pack_f16(fmaf(iv.x, sin2_reduced(t0), v[i]), fmaf(iv.y, sin2_reduced(t1), v[i + 1]));
+    ha[i / 2 + 1] = pack_f16(fmaf(iv.z, sin2_reduced(t2), v[i + 2]), fmaf(iv.w, sin2_reduced(t3), v[i + 3]));
   }
+  return ok;
+}
+
+// The same with sinf, for a chunk where some |alpha y| left that range. Its arrays are its own (sinf's wide-argument
+// path may keep them in local memory; the fast path's registers stay out of it).
+__device__ __forceinline__ void snake16_exact(const float* v, const float* al_s, const float* iv_s, uint32_t* ha) {
+  float y[16];
+  uint32_t h[8];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) y[i] = v[i];
+#pragma unroll 1
+  for (int i = 0; i < 16; i += 2) {
+    const float s0 = sinf(y[i] * al_s[i]), s1 = sinf(y[i + 1] * al_s[i + 1]);
+    h[i / 2] = pack_f16(y[i] + iv_s[i] * s0 * s0, y[i + 1] + iv_s[i + 1] * s1 * s1);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ha[i] = h[i];
 }
 
 template <int KC>
@@ -142,6 +155,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   uint64_t* tfull = empty + nbar;         // [2] accumulator ready
   uint64_t* tempty = tfull + 2;           // [2] accumulator drained
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint32_t* s_amax = tmem_slot + 1;       // max |alpha| bits over the staged activation (NaN above every number)
   // the epilogue's per-column constants, staged once: bias [N], then alpha and inv [cout] (no global loads per tile)
   float* s_bias = reinterpret_cast<float*>(smem + pipe_bytes + CONV_BAR_BYTES);
   float* s_alpha = s_bias + (a.bias != nullptr ? (a.N + 3) / 4 * 4 : 0);
@@ -164,6 +178,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], CONV_EPI_WARPS);
     }
+    *s_amax = 0;
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, 2 * a.sub * a.acc_cols);
@@ -362,88 +377,76 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
     const int part = ew >> 2;                 // the warps on one quarter split the 16-column chunks round robin
     constexpr int PARTS = CONV_EPI_WARPS / 4;
     const int r = quarter * 32 + lane;        // token row of the tile
+    const int rb = r / a.TT, rt = r - rb * a.TT;   // its batch row and timestep within a unit
     {                                         // weights, not written by the previous kernel: before its end
       const int et = tid - 96;
       if (a.bias != nullptr)
         for (int i = et; i < a.N; i += 32 * CONV_EPI_WARPS) s_bias[i] = a.bias[i];
+      uint32_t amax = 0;
       if (a.alpha != nullptr)
         for (int i = et; i < a.cout; i += 32 * CONV_EPI_WARPS) {
-          s_alpha[i] = a.alpha[i];
+          const float al = a.alpha[i];
+          s_alpha[i] = al;
           s_inv[i] = a.inv[i];
+          amax = max(amax, __float_as_uint(al) & 0x7FFFFFFFu);
         }
+      amax = __reduce_max_sync(0xffffffffu, amax);
+      if (lane == 0 && amax != 0) atomicMax(s_amax, amax);
       asm volatile("bar.sync 1, %0;" ::"n"(32 * CONV_EPI_WARPS) : "memory");   // the epilogue warps only
     }
+    const bool act = a.nxt != nullptr && a.alpha != nullptr;
+    // |y| <= 65504 for an fp16 y, so below |alpha| = 32 every |alpha y| is inside sin2_reduced's range: no check
+    const bool chk = act && *s_amax >= __float_as_uint(SIN2_RANGE / 65536.f);
+    const bool cmod = a.cout != a.N;          // a transposed conv's phases share their channel's activation
     pdl_wait();                               // outputs may be buffers the previous kernel still reads
-    const int nchunk = (a.ntile + 15) / 16;
+    const int nchunk = a.ntile >> 4;          // (outside the audio mode N and ntile are multiples of 16)
     const int W = a.sub * nchunk;             // epilogue items of a unit: (sub-tile, 16-column chunk) pairs
-    auto first_item = [&](int itn) {
-      const int f = part - (itn * W) % PARTS;
-      return f < 0 ? f + PARTS : f;
-    };
-    auto res_load = [&](int tl, int g, uint32_t* q) {   // this thread's residual segment of item g of unit tl
-      int b0, t0, n0;
-      coords(tl, &b0, &t0, &n0);
-      const int bb = b0 + r / a.TT, nb = n0 + (g % nchunk) * 16;
-      if (a.res != nullptr && bb < a.rows && nb + 16 <= a.N)
-        ld_global_v8(a.res + (size_t)bb * a.res_bs + (size_t)(t0 + (g / nchunk) * 128 + r % a.TT) * a.res_ts + nb, q);
-    };
-    uint32_t rc[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // the residual of this warp's next item
-    int rc_tile = -1;                         // the unit whose first item rc already holds
+    const long long res_sub = 128LL * a.res_ts, raw_sub = 128LL * a.raw_ts, nxt_sub = 128LL * a.N;
     int it = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
       const int acc = it & 1, use = it >> 1;
+      int b0, t0, n0;
+      coords(tile, &b0, &t0, &n0);
+      const int b = b0 + rb;
+      const bool live = b < a.rows;
+      const long long ts = t0 + rt;
+      // the unit's items are dealt round robin over the warps of this lane quarter, the deal continuing from unit to
+      // unit (a warp left with fewer items of one unit takes more of the next)
+      int f = part - (it * W) % PARTS;
+      if (f < 0) f += PARTS;
+      int s = f / nchunk, ch = f - s * nchunk;
+      // this thread's elements of (sub-tile 0, chunk 0) of the unit; null where nothing is read or written
+      const __half* resp = (a.res != nullptr && live) ? a.res + b * a.res_bs + ts * a.res_ts + n0 : nullptr;
+      uint32_t rc[8] = {0, 0, 0, 0, 0, 0, 0, 0};   // residual of the current item: the first one's is requested
+      if (resp != nullptr && f < W) ld_global_v8(resp + s * res_sub + ch * 16, rc);   // before the accumulator wait
       const bool ok = mbar_wait(&tfull[acc], use & 1, ERR_TIMEOUT_ACCUM, KERNEL_ID_CONV);
       if (!ok) break;                         // (recorded; the MMA has stopped too)
       tc_fence_after();
-      int b0, t0, n0;
-      coords(tile, &b0, &t0, &n0);
-      const int b = b0 + r / a.TT;
-      const bool live = b < a.rows;
       const uint32_t tbase = tmem + acc * a.sub * a.acc_cols + (uint32_t(quarter * 32) << 16);
       if (a.audio != nullptr) {
-        for (int s = part; s < a.sub; s += PARTS) {
+        for (int sb = part; sb < a.sub; sb += PARTS) {
           float v[16];
-          tmem_ld16(tbase + s * a.acc_cols, v);
+          tmem_ld16(tbase + sb * a.acc_cols, v);
           if (live) {
             const float bias = a.bias != nullptr ? a.bias[0] : 0.f;
-            a.audio[(size_t)b * a.audio_bs + t0 + s * 128 + r % a.TT] = tanhf(f16r(v[0] + bias));
+            a.audio[(size_t)b * a.audio_bs + t0 + sb * 128 + rt] = tanhf(f16r(v[0] + bias));
           }
         }
       } else {
-        // the unit's (sub-tile, 16-column chunk) items, dealt round robin over the warps of this lane quarter with
-        // the deal continuing from tile to tile (a warp left with fewer items of one tile takes more of the next).
-        // Each item's residual (one 32-byte load a thread) is requested while the item before it computes -- the
-        // first item of the next tile's during this tile's last.
-        int f = first_item(it);
-        if (rc_tile != tile && f < W) res_load(tile, f, rc);
-        rc_tile = -1;
+        __half* rawp = (a.raw != nullptr && live) ? a.raw + b * a.raw_bs + ts * a.raw_ts + n0 : nullptr;
+        __half* nxtp = (a.nxt != nullptr && live) ? a.nxt + b * a.nxt_bs + a.nxt_off + ts * a.N + n0 : nullptr;
         for (; f < W; f += PARTS) {
+          int s2 = s, ch2 = ch + PARTS;       // the next item of this warp
+          while (ch2 >= nchunk) {
+            ch2 -= nchunk;
+            ++s2;
+          }
           uint32_t rn[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-          if (f + PARTS < W) {
-            res_load(tile, f + PARTS, rn);
-          } else if (tile + (int)gridDim.x < total && first_item(it + 1) < W) {
-            res_load(tile + gridDim.x, first_item(it + 1), rn);
-            rc_tile = tile + gridDim.x;
-          }
-          const int s = f / nchunk, ch = f % nchunk;
-          const int t = t0 + s * 128 + r % a.TT;
-          const uint32_t trow = tbase + s * a.acc_cols;
+          if (resp != nullptr && f + PARTS < W) ld_global_v8(resp + s2 * res_sub + ch2 * 16, rn);
           const int nb = n0 + ch * 16;
-          if (nb >= a.N) {                     // warp-uniform
-#pragma unroll
-            for (int i = 0; i < 8; ++i) rc[i] = rn[i];
-            continue;
-          }
-          const int nn = min(16, a.N - nb);
-          const bool has_res = a.res != nullptr && live && nn == 16;
-          float v[16];
-          tmem_ld16(trow + ch * 16, v);
-          if (nn == 16) {
-            // straight-line fast path (so the 16 columns interleave); a chunk whose activation argument leaves the
-            // range of sin2_reduced is redone with sinf below (warp-uniform)
-            bool ok = true;
-            const bool act = a.nxt != nullptr && a.alpha != nullptr;
-            uint32_t hy[8], ha[8];
+          if (nb < a.N) {                     // warp-uniform: a unit's last tile may reach past N
+            float v[16];
+            tmem_ld16(tbase + s * a.acc_cols + ch * 16, v);
             if (a.bias != nullptr) {
 #pragma unroll
               for (int i = 0; i < 16; i += 4) {
@@ -454,73 +457,41 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
                 v[i + 3] += bv.w;
               }
             }
-            if (has_res) {
+            if (resp != nullptr) {
 #pragma unroll
               for (int i = 0; i < 8; ++i) {
-                const float2 f = unpack_f16(rc[i]);
-                v[2 * i] += f.x;
-                v[2 * i + 1] += f.y;
+                const float2 q = unpack_f16(rc[i]);
+                v[2 * i] += q.x;
+                v[2 * i + 1] += q.y;
               }
             }
+            uint32_t hy[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {                    // fp16 y, and v becomes it (as fp32)
+            for (int i = 0; i < 8; ++i) {     // fp16 y, and v becomes it (as fp32)
               hy[i] = pack_f16(v[2 * i], v[2 * i + 1]);
-              const float2 f = unpack_f16(hy[i]);
-              v[2 * i] = f.x;
-              v[2 * i + 1] = f.y;
+              const float2 q = unpack_f16(hy[i]);
+              v[2 * i] = q.x;
+              v[2 * i + 1] = q.y;
             }
+            if (rawp != nullptr) st_global_v8(rawp + s * raw_sub + ch * 16, hy);   // one 32-byte sector a thread
             if (act) {
-              const int c = nb % a.cout;
-#pragma unroll
-              for (int i = 0; i < 16; i += 4) {
-                const float4 al = *reinterpret_cast<const float4*>(s_alpha + c + i);
-                const float4 iv = *reinterpret_cast<const float4*>(s_inv + c + i);
-                const float al4[4] = {al.x, al.y, al.z, al.w}, iv4[4] = {iv.x, iv.y, iv.z, iv.w};
-                float z[4];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                  const float tt = v[i + k] * al4[k];
-                  ok &= fabsf(tt) < 32768.f;
-                  z[k] = fmaf(iv4[k], sin2_reduced(tt), v[i + k]);
-                }
-                ha[i / 2] = pack_f16(z[0], z[1]);
-                ha[i / 2 + 1] = pack_f16(z[2], z[3]);
+              const int c = cmod ? nb % a.cout : nb;
+              uint32_t ha[8];
+              if (chk) {
+                const bool good = snake16<true>(v, s_alpha + c, s_inv + c, ha);
+                if (!__all_sync(0xffffffffu, good || !live)) snake16_exact(v, s_alpha + c, s_inv + c, ha);   // rare
+              } else {
+                snake16<false>(v, s_alpha + c, s_inv + c, ha);
               }
-            }
-            if (!__all_sync(0xffffffffu, ok || !live)) {   // rare: |alpha y| >= 2^15
-              tmem_ld16(trow + ch * 16, v);
-              if (live) exact_chunk(a, v, b, t, nb, act, hy, ha);
-            }
-            if (live) {                                      // one full 32-byte sector a thread and output
-              if (a.raw != nullptr) st_global_v8(a.raw + (size_t)b * a.raw_bs + (size_t)t * a.raw_ts + nb, hy);
-              if (a.nxt != nullptr) {
-                __half* d = a.nxt + (size_t)b * a.nxt_bs + a.nxt_off + (size_t)t * a.N + nb;
-                if (act)
-                  st_global_v8(d, ha);
-                else
-                  st_global_v8(d, hy);
-              }
-            }
-          } else if (live) {
-            for (int i = 0; i < nn; ++i) {
-              const int n = nb + i;
-              float x = v[i];
-              if (a.bias != nullptr) x += a.bias[n];
-              if (a.res != nullptr) x += __half2float(a.res[(size_t)b * a.res_bs + (size_t)t * a.res_ts + n]);
-              x = f16r(x);
-              if (a.raw != nullptr) a.raw[(size_t)b * a.raw_bs + (size_t)t * a.raw_ts + n] = __float2half_rn(x);
-              if (a.nxt != nullptr) {
-                if (a.alpha != nullptr) {
-                  const int c = n % a.cout;
-                  const float s = sinf(x * a.alpha[c]);
-                  x = x + a.inv[c] * s * s;
-                }
-                a.nxt[(size_t)b * a.nxt_bs + a.nxt_off + (size_t)t * a.N + n] = __float2half_rn(x);
-              }
+              if (nxtp != nullptr) st_global_v8(nxtp + s * nxt_sub + ch * 16, ha);
+            } else if (nxtp != nullptr) {
+              st_global_v8(nxtp + s * nxt_sub + ch * 16, hy);
             }
           }
 #pragma unroll
           for (int i = 0; i < 8; ++i) rc[i] = rn[i];
+          s = s2;
+          ch = ch2;
         }
       }
       tc_fence_before();
@@ -643,6 +614,7 @@ int conv_plan(ConvPlan* p, const void* xin, int rows, int T, int Cin, int ctx, c
 static int conv_check_outputs(const ConvArgs& a) {
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31) == 0; };
   if (a.audio == nullptr && a.raw == nullptr && a.nxt == nullptr) return A8_ERR_ARG;
+  if (a.audio == nullptr && a.N % 16) return A8_ERR_ARG;   // the epilogue stores 16-column segments
   if (a.N % 16 == 0) {
     if (a.raw != nullptr && (!al(a.raw) || a.raw_bs % 16 || a.raw_ts % 16)) return A8_ERR_ALIGN;
     if (a.res != nullptr && (!al(a.res) || a.res_bs % 16 || a.res_ts % 16)) return A8_ERR_ALIGN;
