@@ -197,6 +197,20 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
     *n0 = nt * a.ntile;
   };
 
+  // Ring positions advance with counters (slot, phase) rather than divisions: the producer and MMA loops are single
+  // threads whose every instruction sits between two tensor-core issues.
+  auto advance = [](int& slot, uint32_t& phase, int n) {
+    if (++slot == n) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  };
+  const uint64_t desc_hi = KC == 64 ? ((1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61))
+                                    : ((1ull << 16) | (32ull << 32) | (1ull << 46) | (4ull << 61));
+  // an operand descriptor is desc_hi plus the start address in 16-byte units (14 bits: shared memory < 256 KB), so an
+  // offset into a tile -- a slot, a slab row, a 16-element K step -- is a plain add
+  auto desc_at = [&](uint32_t addr) { return desc_hi | (uint64_t)((addr >> 4) & 0x3FFFu); };
+
   if (a.slab) {
     // ------------------------------------------------------------------ slab mode
     // A (warp 0): for each unit, for each channel block c, the slab of its input rows. B (warp 2): the weight tiles
@@ -209,19 +223,20 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       const uint64_t pol_x = policy_evict_first();
       const int nbox = (a.R + a.hb - 1) / a.hb;
       const uint32_t box_bytes = a.hb * KC * 2, slab_bytes = nbox * box_bytes;
-      int qa = 0;
+      int qa = 0, sa = 0;
+      uint32_t pa = 0;
       bool ok = true;
       pdl_wait();                              // the input rows are the previous kernel's output
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
         int b0, t0, n0;
         coords(tile, &b0, &t0, &n0);
         for (int c = 0; c < cblocks; ++c) {
-          const int sa = qa % a.na;
-          if (!(ok = mbar_wait(&emptyA[sa], ((qa / a.na) & 1) ^ 1, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
+          if (!(ok = mbar_wait(&emptyA[sa], pa ^ 1u, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
           mbar_arrive_expect_tx(&fullA[sa], slab_bytes);
           for (int x = 0; x < nbox; ++x)         // rows past the end of the input read as zeros (and go unused)
             tma_load_3d(slotA(sa) + x * box_bytes, &tmX, &fullA[sa], c * KC, t0 + x * a.hb, b0, pol_x);
           ++qa;
+          advance(sa, pa, a.na);
         }
       }
       // every load issued has landed before the CTA can exit (also after a timeout)
@@ -237,18 +252,19 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
             tma_load_2d(slotB(c * a.taps + j), &tmW, &fullB[0], j * a.Cin + c * KC, 0, pol_w);
         mbar_wait(&fullB[0], 0, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
       } else {
-        int qb = 0;
+        int qb = 0, sb = 0;
+        uint32_t pb = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
           int b0, t0, n0;
           coords(tile, &b0, &t0, &n0);
           for (int c = 0; c < cblocks && ok; ++c) {
             for (int j = 0; j < a.taps; ++j) {
-              const int sb = qb % a.nb;
-              if (!(ok = mbar_wait(&emptyB[sb], ((qb / a.nb) & 1) ^ 1, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
+              if (!(ok = mbar_wait(&emptyB[sb], pb ^ 1u, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
               mbar_arrive_expect_tx(&fullB[sb], b_bytes);
               tma_load_2d(slotB(sb), &tmW, &fullB[sb], j * a.Cin + c * KC, n0, pol_w);
               ++qb;
+              advance(sb, pb, a.nb);
             }
           }
         }
@@ -257,40 +273,49 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       }
     } else if (warp == 1 && lane == 0) {
       const uint32_t idesc = umma_idesc(128, a.ntile, 0);   // fp16 x fp16 -> fp32
-      int qa = 0, qb = 0, it = 0;
+      const uint64_t dA0 = desc_at(smem_u32(slotA(0))), dB0 = desc_at(smem_u32(slotB(0)));
+      const uint32_t a_step = a.a_slot >> 4, b_step = b_bytes >> 4;   // one slot, in descriptor units
+      const uint32_t row_step = (KC * 2) >> 4, tap_step = a.dil * row_step, sub_step = 128 * row_step;
+      int sa = 0, sb = 0, it = 0;
+      uint32_t pa = 0, pb = 0;
       bool ok = !a.resident || mbar_wait(&fullB[0], 0, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
         const int acc = it & 1, use = it >> 1;
         if (!(ok = mbar_wait(&tempty[acc], (use & 1) ^ 1, ERR_TIMEOUT_ACCUM, KERNEL_ID_CONV))) break;
         tc_fence_after();
         const uint32_t d0 = tmem + acc * a.sub * a.acc_cols;
+        uint64_t dBr = dB0;                      // resident weights: tile (c, j) sits at slot c * taps + j
         for (int c = 0; c < cblocks && ok; ++c) {
-          const int sa = qa % a.na;
-          if (!(ok = mbar_wait(&fullA[sa], (qa / a.na) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
+          if (!(ok = mbar_wait(&fullA[sa], pa, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
           tc_fence_after();
-          const uint32_t slab = smem_u32(slotA(sa));
-          for (int j = 0; j < a.taps; ++j) {
-            int sb = c * a.taps + j;
-            if (!a.resident) {
-              sb = qb % a.nb;
-              if (!(ok = mbar_wait(&fullB[sb], (qb / a.nb) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
+          uint64_t da_j = dA0 + sa * a_step;     // tap j reads the slab from row j * dil
+          for (int j = 0; j < a.taps; ++j, da_j += tap_step) {
+            uint64_t db;
+            if (a.resident) {
+              db = dBr;
+              dBr += b_step;
+            } else {
+              if (!(ok = mbar_wait(&fullB[sb], pb, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
               tc_fence_after();
+              db = dB0 + sb * b_step;
             }
-            const uint64_t db = KC == 64 ? umma_desc_sw128(slotB(sb)) : umma_desc_sw64(slotB(sb));
-            for (int s = 0; s < a.sub; ++s) {    // the sub-tiles share the weight tile
-              const uint32_t arow = slab + uint32_t(s * 128 + j * a.dil) * (KC * 2);
-              const uint64_t da = KC == 64 ? umma_desc_sw128_row(arow) : umma_desc_sw64_row(arow);
-              const uint32_t d = d0 + s * a.acc_cols;
+            const uint32_t acc0 = (c | j) != 0;
+            umma_f16(d0, da_j, db, idesc, acc0);
 #pragma unroll
-              for (int k = 0; k < KC / 16; ++k) umma_f16(d, da + 2 * k, db + 2 * k, idesc, (c | j | k) != 0);
+            for (int k = 1; k < KC / 16; ++k) umma_f16(d0, da_j + 2 * k, db + 2 * k, idesc, 1);
+            if (a.sub == 2) {                    // the second 128-step sub-tile shares the weight tile
+              const uint64_t da2 = da_j + sub_step;
+              umma_f16(d0 + a.acc_cols, da2, db, idesc, acc0);
+#pragma unroll
+              for (int k = 1; k < KC / 16; ++k) umma_f16(d0 + a.acc_cols, da2 + 2 * k, db + 2 * k, idesc, 1);
             }
             if (!a.resident) {
               umma_commit(&emptyB[sb]);
-              ++qb;
+              advance(sb, pb, a.nb);
             }
           }
           umma_commit(&emptyA[sa]);
-          ++qa;
+          advance(sa, pa, a.na);
         }
         umma_commit(&tfull[acc]);             // (after a timeout too: the epilogue is not left waiting)
       }
@@ -300,7 +325,8 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       const uint64_t pol_w = policy_evict_last(), pol_x = policy_evict_first();
       // the first tile's weights do not depend on the previous kernel: start them before waiting for it
       const int first = blockIdx.x;
-      int q = 0;                             // k blocks issued so far (all tiles)
+      int q = 0, sq = 0;                     // k blocks issued so far (all tiles); ring slot of the next
+      uint32_t pq = 0;
       bool ok = true;
       if (first < total) {
         int b0, t0, n0;
@@ -314,13 +340,19 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
         for (int i = 0; i < pre; ++i)
           tma_load_3d(tileA(i), &tmX, &full[i], (i % cblocks) * KC, t0 + (i / cblocks) * a.dil, b0, pol_x);
         q = pre;
-        for (int i = pre; i < nkb; ++i) {
-          const int s = i % stages;
-          if (!(ok = mbar_wait(&empty[s], ((i / stages) & 1) ^ 1, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
-          mbar_arrive_expect_tx(&full[s], stage_bytes);
-          tma_load_2d(tileB(s), &tmW, &full[s], (i / cblocks) * a.Cin + (i % cblocks) * KC, n0, pol_w);
-          tma_load_3d(tileA(s), &tmX, &full[s], (i % cblocks) * KC, t0 + (i / cblocks) * a.dil, b0, pol_x);
+        sq = pre == stages ? 0 : pre;
+        pq = pre == stages ? 1u : 0u;
+        for (int i = pre, c = pre % cblocks, j = pre / cblocks; i < nkb; ++i) {
+          if (!(ok = mbar_wait(&empty[sq], pq ^ 1u, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
+          mbar_arrive_expect_tx(&full[sq], stage_bytes);
+          tma_load_2d(tileB(sq), &tmW, &full[sq], j * a.Cin + c * KC, n0, pol_w);
+          tma_load_3d(tileA(sq), &tmX, &full[sq], c * KC, t0 + j * a.dil, b0, pol_x);
           q = i + 1;
+          advance(sq, pq, stages);
+          if (++c == cblocks) {
+            c = 0;
+            ++j;
+          }
         }
       } else {
         pdl_wait();
@@ -328,12 +360,16 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       for (int tile = first + gridDim.x; tile < total && ok; tile += gridDim.x) {
         int b0, t0, n0;
         coords(tile, &b0, &t0, &n0);
-        for (int i = 0; i < nkb; ++i, ++q) {
-          const int s = q % stages;
-          if (!(ok = mbar_wait(&empty[s], ((q / stages) & 1) ^ 1, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
-          mbar_arrive_expect_tx(&full[s], stage_bytes);
-          tma_load_2d(tileB(s), &tmW, &full[s], (i / cblocks) * a.Cin + (i % cblocks) * KC, n0, pol_w);
-          tma_load_3d(tileA(s), &tmX, &full[s], (i % cblocks) * KC, t0 + (i / cblocks) * a.dil, b0, pol_x);
+        for (int i = 0, c = 0, j = 0; i < nkb; ++i, ++q) {
+          if (!(ok = mbar_wait(&empty[sq], pq ^ 1u, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
+          mbar_arrive_expect_tx(&full[sq], stage_bytes);
+          tma_load_2d(tileB(sq), &tmW, &full[sq], j * a.Cin + c * KC, n0, pol_w);
+          tma_load_3d(tileA(sq), &tmX, &full[sq], c * KC, t0 + j * a.dil, b0, pol_x);
+          advance(sq, pq, stages);
+          if (++c == cblocks) {
+            c = 0;
+            ++j;
+          }
         }
       }
       // every load issued has landed before the CTA can exit (also after a timeout)
@@ -343,28 +379,25 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = umma_idesc(128, a.ntile, 0);   // fp16 x fp16 -> fp32
-      int q = 0, it = 0;
+      const uint64_t dA0 = desc_at(smem_u32(tileA(0))), dB0 = desc_at(smem_u32(tileB(0)));
+      const uint32_t st_step = stage_bytes >> 4;
+      int sq = 0, it = 0;
+      uint32_t pq = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
         const int acc = it & 1, use = it >> 1;
         if (!(ok = mbar_wait(&tempty[acc], (use & 1) ^ 1, ERR_TIMEOUT_ACCUM, KERNEL_ID_CONV))) break;
         tc_fence_after();
         const uint32_t d = tmem + acc * a.acc_cols;
-        for (int i = 0; i < nkb; ++i, ++q) {
-          const int s = q % stages;
-          if (!(ok = mbar_wait(&full[s], (q / stages) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
+        for (int i = 0; i < nkb; ++i) {
+          if (!(ok = mbar_wait(&full[sq], pq, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
           tc_fence_after();
-          uint64_t da, db;
-          if constexpr (KC == 64) {
-            da = umma_desc_sw128(tileA(s));
-            db = umma_desc_sw128(tileB(s));
-          } else {
-            da = umma_desc_sw64(tileA(s));
-            db = umma_desc_sw64(tileB(s));
-          }
+          const uint64_t da = dA0 + sq * st_step, db = dB0 + sq * st_step;
+          umma_f16(d, da, db, idesc, i != 0);
 #pragma unroll
-          for (int k = 0; k < KC / 16; ++k) umma_f16(d, da + 2 * k, db + 2 * k, idesc, (i | k) != 0);
-          umma_commit(&empty[s]);
+          for (int k = 1; k < KC / 16; ++k) umma_f16(d, da + 2 * k, db + 2 * k, idesc, 1);
+          umma_commit(&empty[sq]);
+          advance(sq, pq, stages);
         }
         umma_commit(&tfull[acc]);             // (after a timeout too: the epilogue is not left waiting)
       }
