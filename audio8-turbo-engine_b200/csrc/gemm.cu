@@ -400,13 +400,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       pdl_wait();                               // X is produced by the previous kernel
       for (int i = 0; i < pre; ++i) tma_load_2d(tileB(i), &tmX, &full[i], (kb0 + i) * BK, m0, px);
       issued = pre;
-      for (int i = pre; i < nkb; ++i) {
-        const int s = i % stages;
-        if (!mbar_wait(&empty[s], ((i / stages) - 1) & 1, ERR_TIMEOUT_EMPTY, KERNEL_ID_GEMM)) break;
+      // slot and phase by counters: no divisions between this lane's issues (i >= pre only runs when pre == stages)
+      for (int i = pre, s = 0, ph = 0; i < nkb; ++i) {
+        if (!mbar_wait(&empty[s], ph, ERR_TIMEOUT_EMPTY, KERNEL_ID_GEMM)) break;
         mbar_arrive_expect_tx(&full[s], stage_bytes);
         tma_load_2d(tileA(s), &tmW, &full[s], (kb0 + i) * BK, n0, pw);
         tma_load_2d(tileB(s), &tmX, &full[s], (kb0 + i) * BK, m0, px);
         issued = i + 1;
+        if (++s == stages) {
+          s = 0;
+          ph ^= 1;
+        }
       }
       // every requested stage has landed before the slots are reused as epilogue staging (immediate in normal
       // operation: the MMA issuer consumed them; bounded after an error)
@@ -416,14 +420,22 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = umma_idesc(128, a.ntok, 1);
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % stages;
-        if (!mbar_wait(norm ? &normed[s] : &full[s], (i / stages) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_GEMM)) break;
+      // stage s's descriptors are stage 0's plus s stage sizes (the address field counts 16-byte units)
+      const uint64_t da0 = umma_desc_sw128(tileA(0)), db0 = umma_desc_sw128(tileB(0));
+      uint64_t* const bars = norm ? normed : full;
+      for (int i = 0, s = 0, ph = 0; i < nkb; ++i) {
+        if (!mbar_wait(&bars[s], ph, ERR_TIMEOUT_FULL, KERNEL_ID_GEMM)) break;
         tc_fence_after();
-        const uint64_t da = umma_desc_sw128(tileA(s)), db = umma_desc_sw128(tileB(s));
+        const uint64_t off = (uint64_t)(s * (stage_bytes >> 4));
+        const uint64_t da = da0 + off, db = db0 + off;
+        umma_f16(tmem, da, db, idesc, i != 0);
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k) umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, (i | k) != 0);
+        for (int k = 1; k < BK / 16; ++k) umma_f16(tmem, da + 2 * k, db + 2 * k, idesc, 1);
         umma_commit(&empty[s]);
+        if (++s == stages) {
+          s = 0;
+          ph ^= 1;
+        }
       }
       umma_commit(accum);
     }
@@ -447,9 +459,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       rstd_s[j] = r;
     }
     named_bar_sync(1, NORM_WARPS * 32);
-    for (int i = 0; i < nkb; ++i) {
-      const int s = i % stages;
-      if (!mbar_wait(&full[s], (i / stages) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_GEMM)) break;
+    for (int i = 0, s = 0, ph = 0; i < nkb; ++i, s = s + 1 == stages ? 0 : s + 1, ph ^= s == 0) {
+      if (!mbar_wait(&full[s], ph, ERR_TIMEOUT_FULL, KERNEL_ID_GEMM)) break;
       uint8_t* tb = tileB(s);
       const uint4* wk0 = reinterpret_cast<const uint4*>(normw_s + (kb0 + i) * (BK / 2));
       for (int c = nt; c < a.ntok * 8; c += NORM_WARPS * 32) {
@@ -524,11 +535,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = 0.f;
       }
+      int owner = (c * 32) / w, obeg = owner * w;   // owner of the chunk's first column, stepped along it
 #pragma unroll
       for (int g = 0; g < 8; ++g) {
         const int col = c * 32 + g * 4;
-        const int owner = col / w;
-        const uint32_t off = uint32_t(((split * 128 + row) * wp + (col - owner * w)) * 4);
+        while (col >= obeg + w) {
+          ++owner;
+          obeg += w;
+        }
+        const uint32_t off = uint32_t(((split * 128 + row) * wp + (col - obeg)) * 4);
         if (owner == split) {
           *reinterpret_cast<float4*>(recv + off / 4) = make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
         } else {
