@@ -6,7 +6,7 @@
 Workload cfg2 (the default): the full tick at 192 rows -- slow AR step, fast AR, streaming
 codec -- replayed from one CUDA graph; value = frames/s, e2e = the same with each tick's inputs copied in from pinned
 host memory and its audio, tokens and frames copied back; roofline = the codec conv with the largest time. The same
-line then carries `serving`: --serve-streams closed-loop users a GPU (default 1120) for --serve-seconds (default 30)
+line then carries `serving`: --serve-streams closed-loop users a GPU (default 1280, 1536 slots) for --serve-seconds (default 30)
 through the serving loop, with P95 RTF / TTFA and whether the real-time bars held (every rank runs its own replica).
 
 Workloads cfg3 / streams (configs[3], [4] under torchrun): the serving loop (serving.ContinuousBatcher) over an engine of
@@ -615,7 +615,8 @@ def conv_roofline(eng, L, dev, b, args):
 SERVE_METRIC = "real-time streams/GPU at P95 RTF<0.7"
 SERVE_BUCKETS = [1, 2, 4, 6, 8, 12, 16, 20, 24, 28, 32, 40, 48, 56, 64, 72, 80, 88, 96, 104, 112, 120, 128, 144, 160,
                  176, 192, 224, 256, 288, 320, 384, 448, 512, 576, 640, 704, 768, 832, 896, 960, 992, 1024, 1056, 1088,
-                 1120, 1152, 1184, 1216, 1248, 1280, 1408, 1536]
+                 1120, 1152, 1184, 1216, 1248, 1280, 1312, 1344, 1376, 1408, 1440, 1472, 1504, 1536, 1600, 1664, 1728,
+                 1792]
 
 
 def serve_dict(args, world):
@@ -911,11 +912,11 @@ def main():
                          "192 x 4097 logits) between "
                          "cudaProfilerStart/Stop, for ncu "
                          "--profile-from-start off")
-    ap.add_argument("--serve-streams", type=int, default=1120,
+    ap.add_argument("--serve-streams", type=int, default=1280,
                     help="cfg2: closed-loop streams a GPU of the serving run reported under `serving`")
     ap.add_argument("--serve-seconds", type=float, default=30.0,
                     help="cfg2: length of that serving run (0: none)")
-    ap.add_argument("--serve-slots", type=int, default=1280, help="cfg2: max_slots of that serving run")
+    ap.add_argument("--serve-slots", type=int, default=1536, help="cfg2: max_slots of that serving run")
     ap.add_argument("--out-sr", type=int, default=16000,
                     help="cfg3/streams: each stream converted to this rate + PCM16 on the GPU (the worker's "
                          "TTS_OUT_SR; 0 = read back fp32 frames at the codec rate)")
