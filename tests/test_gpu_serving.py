@@ -76,3 +76,60 @@ def test_serving_loop_resampled(a8, serving, tiny_model):
         assert n == -(-r.frames * eng.up * 160 // 441), (r.rid, r.frames, n)
         if r.frames:
             assert len(chunks[0][0]) <= 743 + 90 and np.abs(np.concatenate([y for y, _ in chunks])).max() > 0
+
+
+def test_serving_chain_on_engine(a8, serving, tiny_model):
+    """A code-switch line of three segments (two voices) beside plain requests: every segment of the line runs in the
+    line's one slot, continuations keep the codec state, and each continuation's context is exactly the codes the
+    engine generated for the previous segment in that slot (read back by the loop every tick), from its first kept
+    frame on -- checked against frame_prev recorded after every replay."""
+    gp = dict(do_sample=True, temperature=0.8, top_k=50, top_p=0.95, max_new_tokens=64)
+    eng = a8.FastEngine(tiny_model, StubTokenizer(), gp, max_slots=6, max_seq=512, buckets=[2, 4, 6],
+                        seq_from_env=False, seed=7)
+    eng.capture(log=lambda *a: None)
+    ncb = int(tiny_model.config.num_codebooks)
+    voices = serving.voice_items(2, 12, ncb, seed=5)
+    serving.warm_voices(eng, voices)
+    rec, adm = [], []
+    replay0, admit0 = eng.replay, eng.admit
+
+    def replay(b, *a):
+        replay0(b, *a)
+        torch.cuda.synchronize()
+        rec.append(eng.frame_prev[:b].cpu().clone())
+
+    def admit(slots, reqs):
+        adm.append((len(rec), list(slots), [dict(q) for q in reqs]))
+        return admit0(slots, reqs)
+
+    eng.replay, eng.admit = replay, admit
+    segs = [serving.Segment(text="11 12 13 14 15.", key=voices[0][0], item=voices[0][1], cap=6),
+            serving.Segment(text="21 22 23", key=voices[1][0], item=voices[1][1], cap=5),
+            serving.Segment(text="31 32 33 34", key=voices[0][0], item=voices[0][1], cap=4)]
+    line = serving.Request(rid=100, arrival=0.0, text=segs[0].text, item=segs[0].item, key=segs[0].key, cap=64,
+                           chain=serving.Chain(segs=segs, mode="prev"))
+    plain = [serving.Request(rid=i, arrival=0.002 * i, text=" ".join(str(300 + i + k) for k in range(6 + i)),
+                             item=voices[i % 2][1], key=voices[i % 2][0], cap=4 + i) for i in range(3)]
+    loop = serving.ContinuousBatcher(eng, admit_every=1, admit_batch=4)
+    got = []
+    loop.on_chunk = lambda r, y, final: got.append((y.copy(), final)) if r.rid == 100 else None
+    loop.run([line] + plain)
+    assert a8.device_error()[0] == 0
+    assert line.t_done is not None and line.error is None and got[-1][1]
+    mine = [(t, s[i], q[i]) for t, s, q in adm for i in range(len(s)) if q[i]["text"] in {g.text for g in segs}]
+    assert len({s for _, s, _ in mine}) == 1                       # one slot for the whole line
+    slot = mine[0][1]
+    assert [q.get("keep_voc", False) for _, _, q in mine][:1] == [False] and all(q["keep_voc"] for _, _, q in mine[1:])
+    hist = line.chain.hist
+    assert len(hist) == 2 and [h[1] for h in hist] == [segs[0].text, segs[1].text]
+    for k, (codes, _) in enumerate(hist):
+        t_adm = [t for t, _, q in mine if q["text"] == segs[k].text][-1]          # the try whose codes were kept
+        gen = torch.stack([rec[t_adm + i][slot] for i in range(segs[k].cap)]).numpy()
+        lo = next(o for o in range(len(gen)) if np.array_equal(gen[o], codes[0]))  # leading silence not kept
+        np.testing.assert_array_equal(codes, gen[lo:lo + len(codes)])
+        nxt = [q for _, _, q in mine if q["text"] == segs[k + 1].text][-1]
+        np.testing.assert_array_equal(np.asarray(nxt["ctx_codes"]), codes)      # "prev": the last segment only
+        assert nxt["ctx_text"] == segs[k].text
+    y = np.concatenate([c for c, _ in got])
+    assert y.size > 0 and np.isfinite(y).all() and np.abs(y).max() <= 1.0
+    assert all(r.t_done is not None and r.error is None for r in plain)

@@ -408,3 +408,158 @@ def test_too_long_prompt_reports_error(serving):
     st, errs, finals = _run_flaky(serving, fe, reqs)
     assert errs == {0: ["text too long for TTS_MAX_SEQ"]} and finals[0] == 1 and reqs[0].rejected
     assert st.summary()["failed"] == 0 and st.summary()["rejected"] == 1
+
+
+# ------------------------------------------------------------------------------------------------ code-switch chains
+class ChainEngine:
+    """FastEngine's slot semantics for chains: a row admitted with text T plays the next script queued for T (a list
+    of loud / silent frames, then EOS); tick m after admission generates frame m-1 (frame_prev = [admission id, frame
+    index, 0]) and delivers frame m-2's audio (0.5 loud, 0 silent; tick 1 the silence frame). `too_long`: texts whose
+    prompt does not fit with a context."""
+
+    def __init__(self, scripts, B=4, eos=99, too_long=()):
+        self.B, self.eos, self.up, self.sr = B, eos, 400, 4000          # 0.1 s frames
+        self.scripts = {k: list(v) for k, v in scripts.items()}
+        self.too_long = set(too_long)
+        self.tok_in = torch.zeros(B, dtype=torch.int64)
+        self.audio = torch.zeros(B, self.up)
+        self.frame_prev = torch.zeros(B, 3, dtype=torch.int64)
+        self.row = [None] * B                                             # (admission id, script, tick)
+        self.admissions = []                                              # (slot, admission dict, id)
+
+    def bucket_for(self, n):
+        return self.B
+
+    def admit(self, slots, reqs):
+        out = []
+        for s, q in zip(slots, reqs):
+            if q["text"] in self.too_long and q.get("ctx_codes") is not None:
+                out.append(-1)
+                continue
+            aid = len(self.admissions)
+            self.admissions.append((s, dict(q), aid))
+            self.row[s] = [aid, self.scripts[q["text"]].pop(0), 0]
+            out.append(10)
+        return out
+
+    def replay(self, b):
+        for s in range(b):
+            if self.row[s] is None:
+                continue
+            aid, sc, m = self.row[s]
+            m += 1
+            self.row[s][2] = m
+            if m - 1 < len(sc):
+                self.tok_in[s] = 7
+                self.frame_prev[s] = torch.tensor([aid, m - 1, 0])
+            else:
+                self.tok_in[s] = self.eos
+            self.audio[s].fill_(0.5 if 2 <= m <= len(sc) + 1 and sc[m - 2] else 0.0)
+
+
+def _chain(serving, segs, mode="prev", cap=64, rid=0):
+    ch = serving.Chain(segs=[serving.Segment(text=t, key="v", item=None) for t in segs], mode=mode)
+    return serving.Request(rid=rid, arrival=0.0, text=segs[0], item=None, key="v", cap=cap, chain=ch)
+
+
+def _run_chain(serving, fe, reqs, **kw):
+    got = {}
+    b = serving.ContinuousBatcher(fe, admit_every=1, **kw)
+    b.on_chunk = lambda r, y, final: got.setdefault(r.rid, []).append((y.copy(), final))
+    clk = FakeClock()
+    st = b.run(reqs, clock=clk, sleep=clk.sleep)
+    return b, st, got
+
+
+@pytest.mark.parametrize("mode", ["prev", "full", "none"])
+def test_chain_segments_share_slot_and_context(serving, mode):
+    """Each next segment goes into the line's own slot with the codec state kept and, as its context, the codes the
+    earlier segments generated: the last one ("prev"), all of them ("full") or none; one stream of chunks, final once."""
+    fe = ChainEngine({"one.": [[1, 1, 1]], "two,": [[1, 1]], "three": [[1, 1, 1, 1]]})
+    r = _chain(serving, ["one.", "two,", "three"], mode=mode)
+    _, st, got = _run_chain(serving, fe, [r])
+    assert [a[0] for a in fe.admissions] == [0, 0, 0]
+    assert [a[1].get("keep_voc", False) for a in fe.admissions] == [False, True, True]
+    c1 = np.array([[0, i, 0] for i in range(3)])
+    c2 = np.array([[1, i, 0] for i in range(2)])
+    ctx = [a[1].get("ctx_codes") for a in fe.admissions]
+    txt = [a[1].get("ctx_text") for a in fe.admissions]
+    assert ctx[0] is None
+    if mode == "none":
+        assert ctx[1] is None and ctx[2] is None
+    else:
+        np.testing.assert_array_equal(ctx[1], c1)
+        assert txt[1] == "one."
+        np.testing.assert_array_equal(ctx[2], c2 if mode == "prev" else np.concatenate([c1, c2]))
+        assert txt[2] == ("two," if mode == "prev" else "one. two,")
+    y = np.concatenate([c for c, _ in got[0]])
+    assert [f for _, f in got[0]].count(True) == 1 and got[0][-1][1]
+    assert r.frames == 9 and r.eos and r.t_done is not None and st.summary()["finished"] == 1
+    # every voiced frame went out; the switch "one." -> "two," padded the sentence end to 0.24 s of silence
+    assert int((y == 0.5).sum()) == 9 * 400
+    assert int((y == 0).sum()) >= int(0.24 * 4000) - 40
+
+
+def test_chain_gates_lead_and_tail_silence(serving):
+    """A segment's trailing silence is cut to its punctuation's tail (0.24 s after a sentence end, faded) and the
+    codes kept as context stop that far after its last voiced frame; a continuation's silent lead is cut to the
+    lead (0.16 s) and the frames dropped with it are not context."""
+    fe = ChainEngine({"a.": [[1, 1, 1, 0, 0, 0, 0, 0]], "b": [[0, 0, 0, 0, 1, 1, 0]], "c": [[1]]})
+    r = _chain(serving, ["a.", "b", "c"], mode="prev")
+    _, _, got = _run_chain(serving, fe, [r])
+    y = np.concatenate([c for c, _ in got[0]])
+    loud = np.flatnonzero(y > 0.49)
+    # 3 loud frames, the 0.24 s tail (960 samples, fading to 0 at its end), 0.16 s lead of b, 2 loud frames, b's
+    # trailing silence cut to 0.06 s (no punctuation), then c
+    assert loud[0] == 0 and np.all(y[:1200] == 0.5)
+    assert np.all(y[1200:1200 + 960 + 640] == 0)
+    assert np.all(y[2800:3600] == 0.5)
+    assert np.all(y[3600:3600 + 240] == 0) and np.all(y[3840:4240] == 0.5) and y.size == 4240 + 0
+    ctx_b = fe.admissions[1][1]["ctx_codes"]
+    np.testing.assert_array_equal(ctx_b[:, 1], np.arange(6))          # 3 voiced + ceil(0.24 / 0.1) = 3 tail frames
+    ctx_c = fe.admissions[2][1]["ctx_codes"]
+    # lead of 4 silent frames: 2 kept (0.16 s), 2 dropped; voiced 4, 5; tail ceil(0.06 / 0.1) = 1 frame
+    np.testing.assert_array_equal(ctx_c[:, 1], [2, 3, 4, 5, 6])
+
+
+def test_chain_silent_continuation_sampled_again(serving):
+    """A continuation silent past LEAD_MAX frames is sampled again into the same slot; from CTX_DROP_TRY on without
+    the context; after TRIES_MAX tries the line goes on with what it has. Nothing of a discarded try is sent."""
+    quiet = [0] * (serving.LEAD_MAX + 3)
+    fe = ChainEngine({"x.": [[1, 1]], "y": [quiet, quiet, [0, 1, 1]]})
+    r = _chain(serving, ["x.", "y"])
+    _, _, got = _run_chain(serving, fe, [r])
+    adm = fe.admissions
+    assert [a[1]["text"] for a in adm] == ["x.", "y", "y", "y"] and all(a[0] == 0 for a in adm)
+    assert [a[1].get("ctx_codes") is not None for a in adm] == [False, True, True, False]
+    assert r.chain.tries == 2 and r.eos
+    y = np.concatenate([c for c, _ in got[0]])
+    assert int((y == 0.5).sum()) == 4 * 400                             # 2 + 2 voiced frames, no discarded audio
+
+
+def test_chain_context_too_long_goes_on_without(serving):
+    fe = ChainEngine({"p.": [[1, 1]], "q": [[1]]}, too_long={"q"})
+    r = _chain(serving, ["p.", "q"])
+    _run_chain(serving, fe, [r])
+    assert [a[1]["text"] for a in fe.admissions] == ["p.", "q"]
+    assert fe.admissions[1][1].get("ctx_codes") is None and fe.admissions[1][1]["keep_voc"]
+    assert r.eos and r.error is None
+
+
+def test_chain_cancel_between_segments(serving):
+    """A line cancelled while its next segment waits for admission ends with an empty final chunk and frees the slot."""
+    fe = ChainEngine({"m.": [[1, 1]], "n": [[1]]}, B=1)
+    r = _chain(serving, ["m.", "n"])
+    b = serving.ContinuousBatcher(fe, admit_every=10 ** 6)
+    finals = []
+    b.on_chunk = lambda q, y, final: finals.append(final)
+
+    class Clock(FakeClock):
+        def __call__(self):
+            if r.chain.k == 1 and not r.cancelled:
+                b.cancel(r.rid)
+            return super().__call__()
+
+    clk = Clock()
+    b.run([r], clock=clk, sleep=clk.sleep)
+    assert r.cancelled and finals[-1] and len(fe.admissions) <= 2
