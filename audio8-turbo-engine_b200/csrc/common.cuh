@@ -60,6 +60,32 @@ __device__ __forceinline__ float2 unpack_f16(uint32_t u) {
   return __half22float2(h);
 }
 
+// Packed fp32 pairs (sm_100: add / sub / mul / fma .rn.f32x2 -- two fp32 operations in one instruction, each lane
+// rounded exactly as the scalar instruction)
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+#define A8_F32X2_BINARY(name, op)                                                                       \
+  __device__ __forceinline__ float2 name(float2 a, float2 b) {                                         \
+    float2 d;                                                                                          \
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t" op          \
+        " rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"                                                   \
+        : "=f"(d.x), "=f"(d.y)                                                                         \
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));                                                     \
+    return d;                                                                                          \
+  }
+A8_F32X2_BINARY(fadd2, "add.rn.f32x2")
+A8_F32X2_BINARY(fsub2, "sub.rn.f32x2")
+A8_F32X2_BINARY(fmul2, "mul.rn.f32x2")
+#undef A8_F32X2_BINARY
+__device__ __forceinline__ float2 f2(float x) { return make_float2(x, x); }
+
 // 32-byte global accesses (one full sector a thread; the address must be 32-byte aligned)
 __device__ __forceinline__ void st_global_v8(void* p, const uint32_t* v) {
   asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v[0]), "r"(v[1]), "r"(v[2]),

@@ -87,27 +87,27 @@ __device__ __forceinline__ uint64_t umma_desc_sw64_row(uint32_t addr) {
 // seventh term is below 4e-9 for |r| <= pi/4, so six are kept; odd k swaps sin^2 for cos^2 = 1 - sin^2. Emulated in
 // fp32 with fused multiply-adds against a float64 sin^2 over 2e6 random t a range, the result stays within 1.2e-7
 // absolute for every |t| < 2^22 (the split's error grows as k 2^-48); the epilogue keeps it to |t| < 2^21.
+// Computed two at a time with packed fp32 instructions (each lane rounds as the scalar instruction would).
 constexpr float SIN2_RANGE = 2097152.f;
-__device__ __forceinline__ float sin2_reduced(float t) {
-  const float big = fmaf(t, 0.636619772367581343f, 12582912.0f);
-  const float k = big - 12582912.0f;
-  const uint32_t odd = __float_as_uint(big) & 1u;
-  float r = fmaf(-k, 1.57079637050628662109375f, t);     // pi/2 rounded to fp32
-  r = fmaf(-k, -4.37113900018624283e-8f, r);             // pi/2 minus that
-  const float u = r * r;
-  float p = -4.27556185e-6f;                             // -2^11 / 12!
-  p = fmaf(p, u, 1.41093474e-4f);                        // 2^9 / 10!
-  p = fmaf(p, u, -3.17460317e-3f);                       // -2^7 / 8!
-  p = fmaf(p, u, 4.44444444e-2f);                        // 2^5 / 6!
-  p = fmaf(p, u, -3.33333333e-1f);                       // -2^3 / 4!
-  p = fmaf(p, u, 1.0f);                                  // 2 / 2!
-  const float s2 = u * p;
-  return odd ? 1.0f - s2 : s2;
+__device__ __forceinline__ float2 sin2_reduced2(float2 t) {
+  const float2 big = ffma2(t, f2(0.636619772367581343f), f2(12582912.0f));
+  const float2 k = fsub2(big, f2(12582912.0f));
+  float2 r = ffma2(k, f2(-1.57079637050628662109375f), t);  // -(pi/2 rounded to fp32)
+  r = ffma2(k, f2(4.37113900018624283e-8f), r);             // -(pi/2 minus that)
+  const float2 u = fmul2(r, r);
+  float2 p = ffma2(f2(-4.27556185e-6f), u, f2(1.41093474e-4f));   // -2^11 / 12!, 2^9 / 10!
+  p = ffma2(p, u, f2(-3.17460317e-3f));                           // -2^7 / 8!
+  p = ffma2(p, u, f2(4.44444444e-2f));                            // 2^5 / 6!
+  p = ffma2(p, u, f2(-3.33333333e-1f));                           // -2^3 / 4!
+  p = ffma2(p, u, f2(1.0f));                                      // 2 / 2!
+  const float2 s2 = fmul2(u, p);
+  const float2 c2 = fsub2(f2(1.0f), s2);                          // odd k: cos^2 = 1 - sin^2
+  return make_float2((__float_as_uint(big.x) & 1u) ? c2.x : s2.x, (__float_as_uint(big.y) & 1u) ? c2.y : s2.y);
 }
 
 // The next conv's input of 16 consecutive outputs: ha = fp16(y + inv sin^2(alpha y)) from the fp16-rounded y (as
 // fp32 in v) and the channels' alpha / inv staged in shared memory (16-byte aligned), two values a word. CHECK: also
-// report whether every |alpha y| stayed inside sin2_reduced's range.
+// report whether every |alpha y| stayed inside sin2_reduced2's range.
 template <bool CHECK>
 __device__ __forceinline__ bool snake16(const float* v, const float* al_s, const float* iv_s, uint32_t* ha) {
   bool ok = true;
@@ -115,10 +115,13 @@ __device__ __forceinline__ bool snake16(const float* v, const float* al_s, const
   for (int i = 0; i < 16; i += 4) {
     const float4 al = *reinterpret_cast<const float4*>(al_s + i);
     const float4 iv = *reinterpret_cast<const float4*>(iv_s + i);
-    const float t0 = v[i] * al.x, t1 = v[i + 1] * al.y, t2 = v[i + 2] * al.z, t3 = v[i + 3] * al.w;
-    if (CHECK) ok &= fmaxf(fmaxf(fabsf(t0), fabsf(t1)), fmaxf(fabsf(t2), fabsf(t3))) < SIN2_RANGE;
-    ha[i / 2] = pack_f16(fmaf(iv.x, sin2_reduced(t0), v[i]), fmaf(iv.y, sin2_reduced(t1), v[i + 1]));
-    ha[i / 2 + 1] = pack_f16(fmaf(iv.z, sin2_reduced(t2), v[i + 2]), fmaf(iv.w, sin2_reduced(t3), v[i + 3]));
+    const float2 y0 = make_float2(v[i], v[i + 1]), y1 = make_float2(v[i + 2], v[i + 3]);
+    const float2 t0 = fmul2(y0, make_float2(al.x, al.y)), t1 = fmul2(y1, make_float2(al.z, al.w));
+    if (CHECK) ok &= fmaxf(fmaxf(fabsf(t0.x), fabsf(t0.y)), fmaxf(fabsf(t1.x), fabsf(t1.y))) < SIN2_RANGE;
+    const float2 z0 = ffma2(make_float2(iv.x, iv.y), sin2_reduced2(t0), y0);
+    const float2 z1 = ffma2(make_float2(iv.z, iv.w), sin2_reduced2(t1), y1);
+    ha[i / 2] = pack_f16(z0.x, z0.y);
+    ha[i / 2 + 1] = pack_f16(z1.x, z1.y);
   }
   return ok;
 }
@@ -428,7 +431,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       asm volatile("bar.sync 1, %0;" ::"n"(32 * CONV_EPI_WARPS) : "memory");   // the epilogue warps only
     }
     const bool act = a.nxt != nullptr && a.alpha != nullptr;
-    // |y| <= 65504 for an fp16 y, so below |alpha| = 32 every |alpha y| is inside sin2_reduced's range: no check
+    // |y| <= 65504 for an fp16 y, so below |alpha| = 32 every |alpha y| is inside sin2_reduced2's range: no check
     const bool chk = act && *s_amax >= __float_as_uint(SIN2_RANGE / 65536.f);
     const bool cmod = a.cout != a.N;          // a transposed conv's phases share their channel's activation
     pdl_wait();                               // outputs may be buffers the previous kernel still reads
@@ -484,18 +487,20 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
 #pragma unroll
               for (int i = 0; i < 16; i += 4) {
                 const float4 bv = *reinterpret_cast<const float4*>(s_bias + nb + i);
-                v[i] += bv.x;
-                v[i + 1] += bv.y;
-                v[i + 2] += bv.z;
-                v[i + 3] += bv.w;
+                const float2 p0 = fadd2(make_float2(v[i], v[i + 1]), make_float2(bv.x, bv.y));
+                const float2 p1 = fadd2(make_float2(v[i + 2], v[i + 3]), make_float2(bv.z, bv.w));
+                v[i] = p0.x;
+                v[i + 1] = p0.y;
+                v[i + 2] = p1.x;
+                v[i + 3] = p1.y;
               }
             }
             if (resp != nullptr) {
 #pragma unroll
               for (int i = 0; i < 8; ++i) {
-                const float2 q = unpack_f16(rc[i]);
-                v[2 * i] += q.x;
-                v[2 * i + 1] += q.y;
+                const float2 q = fadd2(make_float2(v[2 * i], v[2 * i + 1]), unpack_f16(rc[i]));
+                v[2 * i] = q.x;
+                v[2 * i + 1] = q.y;
               }
             }
             uint32_t hy[8];
