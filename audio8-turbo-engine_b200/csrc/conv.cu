@@ -291,28 +291,37 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
         for (int c = 0; c < cblocks && ok; ++c) {
           if (!(ok = mbar_wait(&fullA[sa], pa, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
           tc_fence_after();
-          uint64_t da_j = dA0 + sa * a_step;     // tap j reads the slab from row j * dil
-          for (int j = 0; j < a.taps; ++j, da_j += tap_step) {
-            uint64_t db;
-            if (a.resident) {
-              db = dBr;
-              dBr += b_step;
-            } else {
+          // Consecutive MMAs into one accumulator pipeline; switching accumulators between them serialises each
+          // behind the last (measured from one thread, N 16-256: ~51 ns an MMA chained, ~131 ns alternating). With
+          // resident weights each sub-tile therefore takes its whole (tap, K step) run in turn -- the same summation
+          // order a sub-tile had -- and only streamed weight tiles are shared MMA by MMA across sub-tiles.
+          if (a.resident) {
+            for (int s = 0; s < a.sub; ++s) {
+              uint64_t da_j = dA0 + sa * a_step + s * sub_step, db = dBr;   // tile (c, j) at slot c * taps + j
+              const uint32_t d = d0 + s * a.acc_cols;
+              for (int j = 0; j < a.taps; ++j, da_j += tap_step, db += b_step) {
+                umma_f16(d, da_j, db, idesc, (c | j) != 0);
+#pragma unroll
+                for (int k = 1; k < KC / 16; ++k) umma_f16(d, da_j + 2 * k, db + 2 * k, idesc, 1);
+              }
+            }
+            dBr += a.taps * b_step;
+          } else {
+            uint64_t da_j = dA0 + sa * a_step;   // tap j reads the slab from row j * dil
+            for (int j = 0; j < a.taps; ++j, da_j += tap_step) {
               if (!(ok = mbar_wait(&fullB[sb], pb, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
               tc_fence_after();
-              db = dB0 + sb * b_step;
-            }
-            const uint32_t acc0 = (c | j) != 0;
-            umma_f16(d0, da_j, db, idesc, acc0);
+              const uint64_t db = dB0 + sb * b_step;
+              const uint32_t acc0 = (c | j) != 0;
+              umma_f16(d0, da_j, db, idesc, acc0);
 #pragma unroll
-            for (int k = 1; k < KC / 16; ++k) umma_f16(d0, da_j + 2 * k, db + 2 * k, idesc, 1);
-            if (a.sub == 2) {                    // the second 128-step sub-tile shares the weight tile
-              const uint64_t da2 = da_j + sub_step;
-              umma_f16(d0 + a.acc_cols, da2, db, idesc, acc0);
+              for (int k = 1; k < KC / 16; ++k) umma_f16(d0, da_j + 2 * k, db + 2 * k, idesc, 1);
+              if (a.sub == 2) {                  // the second 128-step sub-tile shares the weight tile
+                const uint64_t da2 = da_j + sub_step;
+                umma_f16(d0 + a.acc_cols, da2, db, idesc, acc0);
 #pragma unroll
-              for (int k = 1; k < KC / 16; ++k) umma_f16(d0 + a.acc_cols, da2 + 2 * k, db + 2 * k, idesc, 1);
-            }
-            if (!a.resident) {
+                for (int k = 1; k < KC / 16; ++k) umma_f16(d0 + a.acc_cols, da2 + 2 * k, db + 2 * k, idesc, 1);
+              }
               umma_commit(&emptyB[sb]);
               advance(sb, pb, a.nb);
             }
