@@ -142,6 +142,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int er
   }
 }
 
+// A warp that walks an MMA loop together (so its ring positions and descriptors are warp-uniform) waits with every
+// lane and goes on only if every lane saw the phase (a timeout on any lane stops the whole warp, never a part of it).
+__device__ __forceinline__ bool mbar_wait_all(uint64_t* bar, uint32_t parity, int err, int where) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, where));
+}
+
 // ------------------------------------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_prefetch(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

@@ -274,62 +274,72 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
         for (int i = max(0, qb - a.nb); i < qb; ++i)
           mbar_wait(&fullB[i % a.nb], (i / a.nb) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
       }
-    } else if (warp == 1 && lane == 0) {
+    } else if (warp == 1) {
+      // the whole warp walks the loop (warp-uniform descriptors and ring positions); one elected lane issues the MMAs
+      // and commits (from one lane alone, each commit + barrier wait between MMA groups cost ~20 ns an MMA more)
       const uint32_t idesc = umma_idesc(128, a.ntile, 0);   // fp16 x fp16 -> fp32
       const uint64_t dA0 = desc_at(smem_u32(slotA(0))), dB0 = desc_at(smem_u32(slotB(0)));
       const uint32_t a_step = a.a_slot >> 4, b_step = b_bytes >> 4;   // one slot, in descriptor units
       const uint32_t row_step = (KC * 2) >> 4, tap_step = a.dil * row_step, sub_step = 128 * row_step;
       int sa = 0, sb = 0, it = 0;
       uint32_t pa = 0, pb = 0;
-      bool ok = !a.resident || mbar_wait(&fullB[0], 0, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
+      bool ok = !a.resident || mbar_wait_all(&fullB[0], 0, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
         const int acc = it & 1, use = it >> 1;
-        if (!(ok = mbar_wait(&tempty[acc], (use & 1) ^ 1, ERR_TIMEOUT_ACCUM, KERNEL_ID_CONV))) break;
+        if (!(ok = mbar_wait_all(&tempty[acc], (use & 1) ^ 1, ERR_TIMEOUT_ACCUM, KERNEL_ID_CONV))) break;
         tc_fence_after();
         const uint32_t d0 = tmem + acc * a.sub * a.acc_cols;
         uint64_t dBr = dB0;                      // resident weights: tile (c, j) sits at slot c * taps + j
         for (int c = 0; c < cblocks && ok; ++c) {
-          if (!(ok = mbar_wait(&fullA[sa], pa, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
+          if (!(ok = mbar_wait_all(&fullA[sa], pa, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
           tc_fence_after();
           // Consecutive MMAs into one accumulator pipeline; switching accumulators between them serialises each
           // behind the last (measured from one thread, N 16-256: ~51 ns an MMA chained, ~131 ns alternating). With
           // resident weights each sub-tile therefore takes its whole (tap, K step) run in turn -- the same summation
           // order a sub-tile had -- and only streamed weight tiles are shared MMA by MMA across sub-tiles.
           if (a.resident) {
-            for (int s = 0; s < a.sub; ++s) {
-              uint64_t da_j = dA0 + sa * a_step + s * sub_step, db = dBr;   // tile (c, j) at slot c * taps + j
-              const uint32_t d = d0 + s * a.acc_cols;
-              for (int j = 0; j < a.taps; ++j, da_j += tap_step, db += b_step) {
-                umma_f16(d, da_j, db, idesc, (c | j) != 0);
+            if (elect_one()) {
+              for (int s = 0; s < a.sub; ++s) {
+                uint64_t da_j = dA0 + sa * a_step + s * sub_step, db = dBr;   // tile (c, j) at slot c * taps + j
+                const uint32_t d = d0 + s * a.acc_cols;
+                for (int j = 0; j < a.taps; ++j, da_j += tap_step, db += b_step) {
+                  umma_f16(d, da_j, db, idesc, (c | j) != 0);
 #pragma unroll
-                for (int k = 1; k < KC / 16; ++k) umma_f16(d, da_j + 2 * k, db + 2 * k, idesc, 1);
+                  for (int k = 1; k < KC / 16; ++k) umma_f16(d, da_j + 2 * k, db + 2 * k, idesc, 1);
+                }
               }
             }
+            __syncwarp();
             dBr += a.taps * b_step;
           } else {
             uint64_t da_j = dA0 + sa * a_step;   // tap j reads the slab from row j * dil
             for (int j = 0; j < a.taps; ++j, da_j += tap_step) {
-              if (!(ok = mbar_wait(&fullB[sb], pb, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
+              if (!(ok = mbar_wait_all(&fullB[sb], pb, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
               tc_fence_after();
               const uint64_t db = dB0 + sb * b_step;
               const uint32_t acc0 = (c | j) != 0;
-              umma_f16(d0, da_j, db, idesc, acc0);
+              if (elect_one()) {
+                umma_f16(d0, da_j, db, idesc, acc0);
 #pragma unroll
-              for (int k = 1; k < KC / 16; ++k) umma_f16(d0, da_j + 2 * k, db + 2 * k, idesc, 1);
-              if (a.sub == 2) {                  // the second 128-step sub-tile shares the weight tile
-                const uint64_t da2 = da_j + sub_step;
-                umma_f16(d0 + a.acc_cols, da2, db, idesc, acc0);
+                for (int k = 1; k < KC / 16; ++k) umma_f16(d0, da_j + 2 * k, db + 2 * k, idesc, 1);
+                if (a.sub == 2) {                // the second 128-step sub-tile shares the weight tile
+                  const uint64_t da2 = da_j + sub_step;
+                  umma_f16(d0 + a.acc_cols, da2, db, idesc, acc0);
 #pragma unroll
-                for (int k = 1; k < KC / 16; ++k) umma_f16(d0 + a.acc_cols, da2 + 2 * k, db + 2 * k, idesc, 1);
+                  for (int k = 1; k < KC / 16; ++k) umma_f16(d0 + a.acc_cols, da2 + 2 * k, db + 2 * k, idesc, 1);
+                }
+                umma_commit(&emptyB[sb]);
               }
-              umma_commit(&emptyB[sb]);
+              __syncwarp();
               advance(sb, pb, a.nb);
             }
           }
-          umma_commit(&emptyA[sa]);
+          if (elect_one()) umma_commit(&emptyA[sa]);
+          __syncwarp();
           advance(sa, pa, a.na);
         }
-        umma_commit(&tfull[acc]);             // (after a timeout too: the epilogue is not left waiting)
+        if (elect_one()) umma_commit(&tfull[acc]);   // (after a timeout too: the epilogue is not left waiting)
+        __syncwarp();
       }
     }
   } else if (warp == 0) {
@@ -389,30 +399,32 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
         mbar_wait(&full[i % stages], (i / stages) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = umma_idesc(128, a.ntile, 0);   // fp16 x fp16 -> fp32
-      const uint64_t dA0 = desc_at(smem_u32(tileA(0))), dB0 = desc_at(smem_u32(tileB(0)));
-      const uint32_t st_step = stage_bytes >> 4;
-      int sq = 0, it = 0;
-      uint32_t pq = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
-        const int acc = it & 1, use = it >> 1;
-        if (!(ok = mbar_wait(&tempty[acc], (use & 1) ^ 1, ERR_TIMEOUT_ACCUM, KERNEL_ID_CONV))) break;
+    const uint32_t idesc = umma_idesc(128, a.ntile, 0);   // fp16 x fp16 -> fp32 (the warp walks, one lane issues)
+    const uint64_t dA0 = desc_at(smem_u32(tileA(0))), dB0 = desc_at(smem_u32(tileB(0)));
+    const uint32_t st_step = stage_bytes >> 4;
+    int sq = 0, it = 0;
+    uint32_t pq = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
+      const int acc = it & 1, use = it >> 1;
+      if (!(ok = mbar_wait_all(&tempty[acc], (use & 1) ^ 1, ERR_TIMEOUT_ACCUM, KERNEL_ID_CONV))) break;
+      tc_fence_after();
+      const uint32_t d = tmem + acc * a.acc_cols;
+      for (int i = 0; i < nkb; ++i) {
+        if (!(ok = mbar_wait_all(&full[sq], pq, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
         tc_fence_after();
-        const uint32_t d = tmem + acc * a.acc_cols;
-        for (int i = 0; i < nkb; ++i) {
-          if (!(ok = mbar_wait(&full[sq], pq, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
-          tc_fence_after();
-          const uint64_t da = dA0 + sq * st_step, db = dB0 + sq * st_step;
+        const uint64_t da = dA0 + sq * st_step, db = dB0 + sq * st_step;
+        if (elect_one()) {
           umma_f16(d, da, db, idesc, i != 0);
 #pragma unroll
           for (int k = 1; k < KC / 16; ++k) umma_f16(d, da + 2 * k, db + 2 * k, idesc, 1);
           umma_commit(&empty[sq]);
-          advance(sq, pq, stages);
         }
-        umma_commit(&tfull[acc]);             // (after a timeout too: the epilogue is not left waiting)
+        __syncwarp();
+        advance(sq, pq, stages);
       }
+      if (elect_one()) umma_commit(&tfull[acc]);   // (after a timeout too: the epilogue is not left waiting)
+      __syncwarp();
     }
   }
   if (warp >= 3) {
