@@ -37,6 +37,7 @@ struct ConvArgs {
   // loaded ONCE (a slab) and every tap reads it at row offset j*dil; weights stream through their own ring
   int slab, R, na, nb;
   int resident;             // slab mode, one output tile: all taps x cblocks weight tiles (nb of them) stay loaded
+  int pair;                 // slab mode, streamed weights: CTA pairs (k_conv<KC, true>), half of each weight tile a CTA
   int sub;                  // 128-row sub-tiles a unit (slab mode: 2 share every weight tile; else 1)
   int hb;                   // slab rows a TMA box (a slab of R rows is ceil(R / hb) boxes)
   uint32_t a_slot;          // bytes of one slab slot
@@ -142,13 +143,18 @@ __device__ __forceinline__ void snake16_exact(const float* v, const float* al_s,
   for (int i = 0; i < 8; ++i) ha[i] = h[i];
 }
 
-template <int KC>
+// PAIR: slab mode with streamed weights on CTA pairs (clusters of 2, tcgen05 cta_group::2). The two CTAs take two
+// m-tiles of one n-tile as one 256-row MMA: each loads its own input slab and half of every weight tile (N / 2 rows)
+// and both loads complete bytes on the first CTA's barriers; the first CTA's MMA warp issues for the pair and its
+// commits arrive on both CTAs' barriers; each CTA's epilogue drains its own accumulator rows and arrives on the first
+// CTA's accumulator-drained barrier. Half the MMA instructions, half the weight bytes a CTA.
+template <int KC, bool PAIR>
 __global__ void __launch_bounds__(CONV_THREADS, 1)
     k_conv(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, const ConvArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int stages = a.stages;
-  const uint32_t a_bytes = 128 * KC * 2, b_bytes = a.ntile * KC * 2;
+  const uint32_t a_bytes = 128 * KC * 2, b_bytes = (PAIR ? a.ntile / 2 : a.ntile) * KC * 2;
   const uint32_t stage_bytes = a_bytes + b_bytes;
   // pipeline: `stages` slots of (A, B) -- or, in slab mode, na slab slots then nb weight slots
   const uint32_t pipe_bytes = a.slab ? a.na * a.a_slot + a.nb * b_bytes : stages * stage_bytes;
@@ -169,6 +175,13 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   const int cblocks = a.Cin / KC;
   const int nkb = a.kb_total;
   const int total = a.m_tiles * a.n_tiles;
+  // work items: tiles, or for a pair (m-tile pair, n-tile) -- the second m-tile past the last one is a phantom whose
+  // rows lie beyond the input (zero-filled loads, nothing stored)
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const int cid = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int ncl = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int iters = PAIR ? ((a.m_tiles + 1) / 2) * a.n_tiles : total;
+  auto tile_of = [&](int q) { return PAIR ? ((q / a.n_tiles) * 2 + (int)rank) * a.n_tiles + q % a.n_tiles : q; };
 
   if (tid == 0) {
     tma_prefetch(&tmX);
@@ -179,14 +192,20 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], CONV_EPI_WARPS);
+      mbar_init(&tempty[i], PAIR ? 2 * CONV_EPI_WARPS : CONV_EPI_WARPS);
     }
     *s_amax = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 2 * a.sub * a.acc_cols);
+  if (warp == 1) {
+    if constexpr (PAIR)
+      tmem_alloc_pair(tmem_slot, 2 * a.sub * a.acc_cols);
+    else
+      tmem_alloc(tmem_slot, 2 * a.sub * a.acc_cols);
+  }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();     // the peer's barriers exist before anything signals them
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_launch();
@@ -230,21 +249,30 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       uint32_t pa = 0;
       bool ok = true;
       pdl_wait();                              // the input rows are the previous kernel's output
-      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+      for (int q = cid; q < iters && ok; q += ncl) {
         int b0, t0, n0;
-        coords(tile, &b0, &t0, &n0);
+        coords(tile_of(q), &b0, &t0, &n0);
         for (int c = 0; c < cblocks; ++c) {
           if (!(ok = mbar_wait(&emptyA[sa], pa ^ 1u, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
-          mbar_arrive_expect_tx(&fullA[sa], slab_bytes);
-          for (int x = 0; x < nbox; ++x)         // rows past the end of the input read as zeros (and go unused)
-            tma_load_3d(slotA(sa) + x * box_bytes, &tmX, &fullA[sa], c * KC, t0 + x * a.hb, b0, pol_x);
+          if constexpr (PAIR) {                  // both slabs count on the first CTA's barrier
+            if (rank == 0) mbar_arrive_expect_tx(&fullA[sa], 2 * slab_bytes);
+            const uint32_t mb = dsmem_addr(smem_u32(&fullA[sa]), 0);
+            for (int x = 0; x < nbox; ++x)
+              tma_load_3d_pair(slotA(sa) + x * box_bytes, &tmX, mb, c * KC, t0 + x * a.hb, b0, pol_x);
+          } else {
+            mbar_arrive_expect_tx(&fullA[sa], slab_bytes);
+            for (int x = 0; x < nbox; ++x)       // rows past the end of the input read as zeros (and go unused)
+              tma_load_3d(slotA(sa) + x * box_bytes, &tmX, &fullA[sa], c * KC, t0 + x * a.hb, b0, pol_x);
+          }
           ++qa;
           advance(sa, pa, a.na);
         }
       }
-      // every load issued has landed before the CTA can exit (also after a timeout)
-      for (int i = max(0, qa - a.na); i < qa; ++i)
-        mbar_wait(&fullA[i % a.na], (i / a.na) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
+      // every load issued has landed before the CTA can exit (also after a timeout); a pair's second CTA knows it
+      // from the first, which waited for both slabs, at the closing cluster barrier
+      if (!PAIR || rank == 0)
+        for (int i = max(0, qa - a.na); i < qa; ++i)
+          mbar_wait(&fullA[i % a.na], (i / a.na) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
     } else if (warp == 2 && lane == 0) {
       // weights are never written by a previous kernel: no wait for it
       const uint64_t pol_w = policy_evict_last();
@@ -258,33 +286,40 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
         int qb = 0, sb = 0;
         uint32_t pb = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        for (int q = cid; q < iters && ok; q += ncl) {
           int b0, t0, n0;
-          coords(tile, &b0, &t0, &n0);
+          coords(tile_of(q), &b0, &t0, &n0);
           for (int c = 0; c < cblocks && ok; ++c) {
             for (int j = 0; j < a.taps; ++j) {
               if (!(ok = mbar_wait(&emptyB[sb], pb ^ 1u, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
-              mbar_arrive_expect_tx(&fullB[sb], b_bytes);
-              tma_load_2d(slotB(sb), &tmW, &fullB[sb], j * a.Cin + c * KC, n0, pol_w);
+              if constexpr (PAIR) {              // this CTA's half of the tile's output channels
+                if (rank == 0) mbar_arrive_expect_tx(&fullB[sb], 2 * b_bytes);
+                tma_load_2d_pair(slotB(sb), &tmW, dsmem_addr(smem_u32(&fullB[sb]), 0), j * a.Cin + c * KC,
+                                 n0 + (int)rank * (a.ntile / 2), pol_w);
+              } else {
+                mbar_arrive_expect_tx(&fullB[sb], b_bytes);
+                tma_load_2d(slotB(sb), &tmW, &fullB[sb], j * a.Cin + c * KC, n0, pol_w);
+              }
               ++qb;
               advance(sb, pb, a.nb);
             }
           }
         }
-        for (int i = max(0, qb - a.nb); i < qb; ++i)
-          mbar_wait(&fullB[i % a.nb], (i / a.nb) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
+        if (!PAIR || rank == 0)
+          for (int i = max(0, qb - a.nb); i < qb; ++i)
+            mbar_wait(&fullB[i % a.nb], (i / a.nb) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
       }
-    } else if (warp == 1) {
+    } else if (warp == 1 && (!PAIR || rank == 0)) {
       // the whole warp walks the loop (warp-uniform descriptors and ring positions); one elected lane issues the MMAs
       // and commits (from one lane alone, each commit + barrier wait between MMA groups cost ~20 ns an MMA more)
-      const uint32_t idesc = umma_idesc(128, a.ntile, 0);   // fp16 x fp16 -> fp32
+      const uint32_t idesc = umma_idesc(PAIR ? 256 : 128, a.ntile, 0);   // fp16 x fp16 -> fp32
       const uint64_t dA0 = desc_at(smem_u32(slotA(0))), dB0 = desc_at(smem_u32(slotB(0)));
       const uint32_t a_step = a.a_slot >> 4, b_step = b_bytes >> 4;   // one slot, in descriptor units
       const uint32_t row_step = (KC * 2) >> 4, tap_step = a.dil * row_step, sub_step = 128 * row_step;
       int sa = 0, sb = 0, it = 0;
       uint32_t pa = 0, pb = 0;
       bool ok = !a.resident || mbar_wait_all(&fullB[0], 0, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
-      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
+      for (int q = cid; q < iters && ok; q += ncl, ++it) {
         const int acc = it & 1, use = it >> 1;
         if (!(ok = mbar_wait_all(&tempty[acc], (use & 1) ^ 1, ERR_TIMEOUT_ACCUM, KERNEL_ID_CONV))) break;
         tc_fence_after();
@@ -319,26 +354,43 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
               const uint64_t db = dB0 + sb * b_step;
               const uint32_t acc0 = (c | j) != 0;
               if (elect_one()) {
-                umma_f16(d0, da_j, db, idesc, acc0);
+                if constexpr (PAIR) {            // (the host pairs CTAs only with one 128-step sub-tile)
+                  umma_f16_pair(d0, da_j, db, idesc, acc0);
 #pragma unroll
-                for (int k = 1; k < KC / 16; ++k) umma_f16(d0, da_j + 2 * k, db + 2 * k, idesc, 1);
-                if (a.sub == 2) {                // the second 128-step sub-tile shares the weight tile
-                  const uint64_t da2 = da_j + sub_step;
-                  umma_f16(d0 + a.acc_cols, da2, db, idesc, acc0);
+                  for (int k = 1; k < KC / 16; ++k) umma_f16_pair(d0, da_j + 2 * k, db + 2 * k, idesc, 1);
+                  umma_commit_pair(&emptyB[sb]);
+                } else {
+                  umma_f16(d0, da_j, db, idesc, acc0);
 #pragma unroll
-                  for (int k = 1; k < KC / 16; ++k) umma_f16(d0 + a.acc_cols, da2 + 2 * k, db + 2 * k, idesc, 1);
+                  for (int k = 1; k < KC / 16; ++k) umma_f16(d0, da_j + 2 * k, db + 2 * k, idesc, 1);
+                  if (a.sub == 2) {              // the second 128-step sub-tile shares the weight tile
+                    const uint64_t da2 = da_j + sub_step;
+                    umma_f16(d0 + a.acc_cols, da2, db, idesc, acc0);
+#pragma unroll
+                    for (int k = 1; k < KC / 16; ++k) umma_f16(d0 + a.acc_cols, da2 + 2 * k, db + 2 * k, idesc, 1);
+                  }
+                  umma_commit(&emptyB[sb]);
                 }
-                umma_commit(&emptyB[sb]);
               }
               __syncwarp();
               advance(sb, pb, a.nb);
             }
           }
-          if (elect_one()) umma_commit(&emptyA[sa]);
+          if (elect_one()) {
+            if constexpr (PAIR)
+              umma_commit_pair(&emptyA[sa]);
+            else
+              umma_commit(&emptyA[sa]);
+          }
           __syncwarp();
           advance(sa, pa, a.na);
         }
-        if (elect_one()) umma_commit(&tfull[acc]);   // (after a timeout too: the epilogue is not left waiting)
+        if (elect_one()) {                       // (after a timeout too: the epilogue is not left waiting)
+          if constexpr (PAIR)
+            umma_commit_pair(&tfull[acc]);
+          else
+            umma_commit(&tfull[acc]);
+        }
         __syncwarp();
       }
     }
@@ -460,10 +512,10 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
     const int W = a.sub * nchunk;             // epilogue items of a unit: (sub-tile, 16-column chunk) pairs
     const long long res_sub = 128LL * a.res_ts, raw_sub = 128LL * a.raw_ts, nxt_sub = 128LL * a.N;
     int it = 0;
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+    for (int q = cid; q < iters; q += ncl, ++it) {
       const int acc = it & 1, use = it >> 1;
       int b0, t0, n0;
-      coords(tile, &b0, &t0, &n0);
+      coords(tile_of(q), &b0, &t0, &n0);
       const int b = b0 + rb;
       const bool live = b < a.rows;
       const long long ts = t0 + rt;
@@ -555,12 +607,22 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (lane == 0) {
+        if constexpr (PAIR)                   // the pair's MMA warp (first CTA) waits for both CTAs' drains
+          mbar_arrive_cluster(dsmem_addr(smem_u32(&tempty[acc]), 0));
+        else
+          mbar_arrive(&tempty[acc]);
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, 2 * a.sub * a.acc_cols);
+  if constexpr (PAIR) {
+    cluster_sync();                       // no CTA leaves while its peer may still signal its barriers
+    if (warp == 1) tmem_dealloc_pair(tmem, 2 * a.sub * a.acc_cols);
+  } else {
+    if (warp == 1) tmem_dealloc(tmem, 2 * a.sub * a.acc_cols);
+  }
 }
 
 // ------------------------------------------------------------------------------------------------ context shift
@@ -648,6 +710,13 @@ int conv_plan(ConvPlan* p, const void* xin, int rows, int T, int Cin, int ctx, c
       a.na = 2;
       a.nb = std::min(16, (budget - a.na * (int)a.a_slot) / b_bytes);
       if (a.nb < 2) return A8_ERR_SIZE;                      // (not reached with the decoder's shapes)
+      // Streamed weights: CTA pairs, each CTA holding half of every weight tile (so the ring holds twice the MMA
+      // work in the same bytes) and one 256-row MMA instruction doing both CTAs' rows. Measured on the k7 convs at
+      // Cin 192 / 384: ~8 % faster; the 2-tap transposed conv is not (kept on single CTAs).
+      if (a.sub == 1 && a.ntile % 32 == 0 && taps > 2) {
+        a.pair = 1;
+        a.nb = std::min(24, (budget - a.na * (int)a.a_slot) / (b_bytes / 2));
+      }
     }
   }
   const CUtensorMapSwizzle sw = a.KC == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
@@ -655,7 +724,7 @@ int conv_plan(ConvPlan* p, const void* xin, int rows, int T, int Cin, int ctx, c
                          (uint64_t)(ctx + T) * Cin * 2, a.KC, a.slab ? a.hb : a.TT, a.slab ? 1 : a.TB, sw);
   if (rc) return rc;
   rc = encode_map_2d(&p->tmW, w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)taps * Cin, N, (uint64_t)taps * Cin * 2,
-                     a.KC, a.ntile, sw);
+                     a.KC, a.pair ? a.ntile / 2 : a.ntile, sw);
   if (rc) return rc;
   static int sms = 0;
   if (sms == 0) {
@@ -664,8 +733,14 @@ int conv_plan(ConvPlan* p, const void* xin, int rows, int T, int Cin, int ctx, c
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
   }
   const int total = a.m_tiles * a.n_tiles;
-  p->grid = dim3(std::min(total, sms));
-  p->smem = (a.slab ? a.na * a.a_slot + a.nb * b_bytes : a.stages * stage_bytes) + 1024 + CONV_BAR_BYTES;
+  if (a.pair) {
+    const int pairs = (a.m_tiles + 1) / 2 * a.n_tiles;
+    p->grid = dim3(2 * std::min(pairs, sms / 2));
+  } else {
+    p->grid = dim3(std::min(total, sms));
+  }
+  p->smem = (a.slab ? a.na * a.a_slot + a.nb * (a.pair ? b_bytes / 2 : b_bytes) : a.stages * stage_bytes) + 1024 +
+            CONV_BAR_BYTES;
   return A8_OK;
 }
 
@@ -698,28 +773,29 @@ int conv_launch(const ConvPlan* p, cudaStream_t s) {
   cfg.dynamicSmemBytes = p->smem + params;
   if (cfg.dynamicSmemBytes > 227 * 1024) return A8_ERR_SIZE;
   cfg.stream = s;
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
+  at[1].id = cudaLaunchAttributeClusterDimension;   // CTA pairs: clusters of 2
+  at[1].val.clusterDim.x = 2;
+  at[1].val.clusterDim.y = 1;
+  at[1].val.clusterDim.z = 1;
   cfg.attrs = at;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = a.pair ? 2 : 1;
   ++g_launches;
-  cudaError_t e;
-  if (p->args.KC == 64) {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(k_conv<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-      attr = true;
-    }
-    e = cudaLaunchKernelEx(&cfg, k_conv<64>, p->tmX, p->tmW, p->args);
-  } else {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(k_conv<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-      attr = true;
-    }
-    e = cudaLaunchKernelEx(&cfg, k_conv<32>, p->tmX, p->tmW, p->args);
+  auto run = [&](auto kern) {
+    static_assert(sizeof(kern) > 0, "");
+    return cudaLaunchKernelEx(&cfg, kern, p->tmX, p->tmW, p->args);
+  };
+  static bool attr[4] = {false, false, false, false};
+  const int v = (a.KC == 64 ? 0 : 2) + (a.pair ? 1 : 0);
+  void (*kern)(CUtensorMap, CUtensorMap, ConvArgs) =
+      v == 0 ? k_conv<64, false> : v == 1 ? k_conv<64, true> : v == 2 ? k_conv<32, false> : k_conv<32, true>;
+  if (!attr[v]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    attr[v] = true;
   }
+  const cudaError_t e = run(kern);
   return e == cudaSuccess ? A8_OK : A8_ERR_CUDA;
 }
 

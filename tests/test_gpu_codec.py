@@ -123,6 +123,8 @@ CONV_CASES = [
     ("trans_s8", 256, 128, 0, 1, True, 8, True, 4, 33, False),
     ("k7_wide", 384, 384, 7, 1, False, 1, True, 256, 2, False),
     ("many_tiles", 192, 192, 7, 3, False, 1, True, 1024, 40, False),
+    # streamed weights on CTA pairs with an odd number of 128-step tiles (the last pair's second tile is beyond the rows)
+    ("pair_odd_tiles", 192, 192, 7, 1, False, 1, True, 128, 3, False),
 ]
 
 
