@@ -244,6 +244,25 @@ def test_attention_gqa_ragged(L, ws):
     assert rel(out, ref) < 1e-2
 
 
+@pytest.mark.parametrize("nq,nkv", [(14, 2), (8, 8)])
+def test_attention_short_window(L, ws, nq, nkv):
+    """Windows of at most 32 keys (the fast AR's 2..10 positions): against the oracle, with and without a row map (two
+    query rows a cache row, as the fast AR's first pass), and the result independent of the max_len bound given."""
+    g = torch.Generator().manual_seed(11 + nq)
+    hd, clen = 64, 40
+    lens = torch.tensor([1, 2, 3, 5, 9, 10, 10, 16, 31, 32, 7, 1])
+    b = len(lens)
+    q = rnd(g, b, nq, hd)
+    kc, vc = rnd(g, 2, b + 3, nkv, clen, hd), rnd(g, 2, b + 3, nkv, clen, hd)
+    out = attention(L, ws, q.cuda(), kc.cuda(), vc.cuda(), lens, max_len=32)
+    assert rel(out, R.decode_attention(q.float(), kc[1].float(), vc[1].float(), lens)) < 1e-2
+    wide = attention(L, ws, q.cuda(), kc.cuda(), vc.cuda(), lens, max_len=clen)
+    assert rel(out, wide) < 1e-2
+    rowmap = torch.arange(b) // 2                        # the fast AR's first pass: two query rows a cache row
+    out = attention(L, ws, q.cuda(), kc.cuda(), vc.cuda(), lens, rowmap, max_len=32)
+    assert rel(out, R.decode_attention(q.float(), kc[1].float(), vc[1].float(), lens, rowmap=rowmap)) < 1e-2
+
+
 def test_attention_mha_ring(L, ws):
     g = torch.Generator().manual_seed(4)
     q = rnd(g, 7, 8, 128)
