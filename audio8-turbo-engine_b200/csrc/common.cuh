@@ -318,9 +318,11 @@ __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t nco
 __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
-// arrive on an mbarrier of another CTA of the cluster (its shared::cluster address)
+// arrive on an mbarrier of another CTA of the cluster (its shared::cluster address), with the instruction's default
+// semantics: an epilogue that has finished its tensor-memory loads (tcgen05.wait::ld, fence::before_thread_sync)
+// hands the accumulator back this way, as the cluster's MMA side orders its own use with fence::after_thread_sync
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
