@@ -6,7 +6,7 @@
 Workload cfg2 (the default): the full tick at 192 rows -- slow AR step, fast AR, streaming
 codec -- replayed from one CUDA graph; value = frames/s, e2e = the same with each tick's inputs copied in from pinned
 host memory and its audio, tokens and frames copied back; roofline = the codec conv with the largest time. The same
-line then carries `serving`: --serve-streams closed-loop users a GPU (default 1280, 1536 slots) for --serve-seconds (default 30)
+line then carries `serving`: --serve-streams closed-loop users a GPU (default 1408, 1536 slots) for --serve-seconds (default 30)
 through the serving loop, with P95 RTF / TTFA and whether the real-time bars held (every rank runs its own replica).
 
 Workloads cfg3 / streams (configs[3], [4] under torchrun): the serving loop (serving.ContinuousBatcher) over an engine of
@@ -912,7 +912,7 @@ def main():
                          "192 x 4097 logits) between "
                          "cudaProfilerStart/Stop, for ncu "
                          "--profile-from-start off")
-    ap.add_argument("--serve-streams", type=int, default=1280,
+    ap.add_argument("--serve-streams", type=int, default=1408,
                     help="cfg2: closed-loop streams a GPU of the serving run reported under `serving`")
     ap.add_argument("--serve-seconds", type=float, default=30.0,
                     help="cfg2: length of that serving run (0: none)")
