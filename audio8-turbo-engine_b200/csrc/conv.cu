@@ -26,6 +26,8 @@ constexpr int KERNEL_ID_CONV = 4;
 constexpr int CONV_EPI_WARPS = 16;
 constexpr int CONV_THREADS = 96 + 32 * CONV_EPI_WARPS;   // A producer, MMA, B producer, epilogue
 constexpr int CONV_BAR_BYTES = 512;                        // mbarriers + the TMEM address, after the pipeline
+constexpr int ETMA_WARP_BYTES = 4096;                      // TMA epilogue: residual[2] | raw | next input, 1 KB each
+constexpr int ETMA_BYTES = CONV_EPI_WARPS * ETMA_WARP_BYTES + 128;   // every epilogue warp's staging + alignment
 
 struct ConvArgs {
   int rows, T, Cin, N, taps, dil, ctx;
@@ -38,6 +40,7 @@ struct ConvArgs {
   int slab, R, na, nb;
   int resident;             // slab mode, one output tile: all taps x cblocks weight tiles (nb of them) stay loaded
   int pair;                 // slab mode, streamed weights: CTA pairs (k_conv<KC, true>), half of each weight tile a CTA
+  int etma;                 // 1x1 convs: residual in / outputs out by TMA boxes (k_conv<KC, false, true>)
   int sub;                  // 128-row sub-tiles a unit (slab mode: 2 share every weight tile; else 1)
   int hb;                   // slab rows a TMA box (a slab of R rows is ceil(R / hb) boxes)
   uint32_t a_slot;          // bytes of one slab slot
@@ -148,9 +151,14 @@ __device__ __forceinline__ void snake16_exact(const float* v, const float* al_s,
 // and both loads complete bytes on the first CTA's barriers; the first CTA's MMA warp issues for the pair and its
 // commits arrive on both CTAs' barriers; each CTA's epilogue drains its own accumulator rows and arrives on the first
 // CTA's accumulator-drained barrier. Half the MMA instructions, half the weight bytes a CTA.
-template <int KC, bool PAIR>
+// ETMA: 1x1 convs (no slab, one 128-step sub-tile, at least 32 steps a unit): each epilogue warp moves its item's 32
+// token rows x 16 channels by TMA through its own shared-memory staging -- the residual in (one item ahead), the raw
+// output and the next conv's input out -- a box of whole lines instead of 32 scattered 32-byte sectors a warp access.
+template <int KC, bool PAIR, bool ETMA>
 __global__ void __launch_bounds__(CONV_THREADS, 1)
-    k_conv(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, const ConvArgs a) {
+    k_conv(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+           const __grid_constant__ CUtensorMap tmR, const __grid_constant__ CUtensorMap tmO,
+           const __grid_constant__ CUtensorMap tmN, const ConvArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int stages = a.stages;
@@ -169,6 +177,9 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   float* s_bias = reinterpret_cast<float*>(smem + pipe_bytes + CONV_BAR_BYTES);
   float* s_alpha = s_bias + (a.bias != nullptr ? (a.N + 3) / 4 * 4 : 0);
   float* s_inv = s_alpha + (a.cout + 3) / 4 * 4;
+  uint64_t* rbar = reinterpret_cast<uint64_t*>(tmem_slot + 2);   // ETMA: [epilogue warp][2] residual boxes landed
+  uint8_t* estage = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(s_inv + (a.cout + 3) / 4 * 4) + 127) &
+                                               ~uintptr_t(127));
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tiles_t = a.T / (a.TT * a.sub);
@@ -195,6 +206,8 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       mbar_init(&tempty[i], PAIR ? 2 * CONV_EPI_WARPS : CONV_EPI_WARPS);
     }
     *s_amax = 0;
+    if constexpr (ETMA)
+      for (int i = 0; i < 2 * CONV_EPI_WARPS; ++i) mbar_init(&rbar[i], 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -510,108 +523,215 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
     pdl_wait();                               // outputs may be buffers the previous kernel still reads
     const int nchunk = a.ntile >> 4;          // (outside the audio mode N and ntile are multiples of 16)
     const int W = a.sub * nchunk;             // epilogue items of a unit: (sub-tile, 16-column chunk) pairs
-    const long long res_sub = 128LL * a.res_ts, raw_sub = 128LL * a.raw_ts, nxt_sub = 128LL * a.N;
-    int it = 0;
-    for (int q = cid; q < iters; q += ncl, ++it) {
-      const int acc = it & 1, use = it >> 1;
-      int b0, t0, n0;
-      coords(tile_of(q), &b0, &t0, &n0);
-      const int b = b0 + rb;
-      const bool live = b < a.rows;
-      const long long ts = t0 + rt;
-      // the unit's items are dealt round robin over the warps of this lane quarter, the deal continuing from unit to
-      // unit (a warp left with fewer items of one unit takes more of the next)
-      int f = part - (it * W) % PARTS;
-      if (f < 0) f += PARTS;
-      int s = f / nchunk, ch = f - s * nchunk;
-      // this thread's elements of (sub-tile 0, chunk 0) of the unit; null where nothing is read or written
-      const __half* resp = (a.res != nullptr && live) ? a.res + b * a.res_bs + ts * a.res_ts + n0 : nullptr;
-      uint32_t rc[8] = {0, 0, 0, 0, 0, 0, 0, 0};   // residual of the current item: the first one's is requested
-      if (resp != nullptr && f < W) ld_global_v8(resp + s * res_sub + ch * 16, rc);   // before the accumulator wait
-      const bool ok = mbar_wait(&tfull[acc], use & 1, ERR_TIMEOUT_ACCUM, KERNEL_ID_CONV);
-      if (!ok) break;                         // (recorded; the MMA has stopped too)
-      tc_fence_after();
-      const uint32_t tbase = tmem + acc * a.sub * a.acc_cols + (uint32_t(quarter * 32) << 16);
-      if (a.audio != nullptr) {
-        for (int sb = part; sb < a.sub; sb += PARTS) {
+    if constexpr (ETMA) {
+      uint8_t* wst = estage + ew * ETMA_WARP_BYTES;   // residual[2] | raw | next input
+      uint64_t* rbw = rbar + 2 * ew;
+      const uint64_t pol = policy_evict_first();
+      const bool has_res = a.res != nullptr;
+      const int row0 = quarter * 32;
+      uint32_t rq = 0, rd = 0;                        // residual boxes requested / consumed by this warp
+      int it = 0;
+      for (int q = cid; q < iters; q += ncl, ++it) {
+        const int acc = it & 1, use = it >> 1;
+        int b0, t0, n0;
+        coords(tile_of(q), &b0, &t0, &n0);
+        const int bw = b0 + row0 / a.TT, tw = t0 + row0 % a.TT;   // the warp's box: 32 steps of one batch row
+        const bool live = bw < a.rows;                 // (warp-uniform; rows past the input are clipped by TMA)
+        int f = part - (it * W) % PARTS;
+        if (f < 0) f += PARTS;
+        auto request = [&](int item) {                 // residual box of an item into the next staging slot
+          if (lane == 0) {
+            uint64_t* bar = &rbw[rq & 1];
+            mbar_arrive_expect_tx(bar, 1024);
+            tma_load_3d(wst + (rq & 1) * 1024, &tmR, bar, n0 + item * 16, tw, bw, pol);
+          }
+          ++rq;
+        };
+        if (has_res && f < W) request(f);              // before the accumulator wait
+        const bool ok = mbar_wait(&tfull[acc], use & 1, ERR_TIMEOUT_ACCUM, KERNEL_ID_CONV);
+        if (!ok) break;                                // (recorded; the MMA has stopped too)
+        tc_fence_after();
+        const uint32_t tbase = tmem + acc * a.acc_cols + (uint32_t(row0) << 16);
+        for (; f < W; f += PARTS) {
+          // the next item's residual goes to the slot the previous item's came from (read into registers already)
+          if (has_res && f + PARTS < W) request(f + PARTS);
+          const int nb = n0 + f * 16;
           float v[16];
-          tmem_ld16(tbase + sb * a.acc_cols, v);
-          if (live) {
-            const float bias = a.bias != nullptr ? a.bias[0] : 0.f;
-            a.audio[(size_t)b * a.audio_bs + t0 + sb * 128 + rt] = tanhf(f16r(v[0] + bias));
+          tmem_ld16(tbase + f * 16, v);
+          if (a.bias != nullptr) {
+#pragma unroll
+            for (int i = 0; i < 16; i += 4) {
+              const float4 bv = *reinterpret_cast<const float4*>(s_bias + nb + i);
+              const float2 p0 = fadd2(make_float2(v[i], v[i + 1]), make_float2(bv.x, bv.y));
+              const float2 p1 = fadd2(make_float2(v[i + 2], v[i + 3]), make_float2(bv.z, bv.w));
+              v[i] = p0.x;
+              v[i + 1] = p0.y;
+              v[i + 2] = p1.x;
+              v[i + 3] = p1.y;
+            }
+          }
+          if (has_res) {
+            mbar_wait(&rbw[rd & 1], (rd >> 1) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
+            const uint4* src = reinterpret_cast<const uint4*>(wst + (rd & 1) * 1024 + lane * 32);
+            const uint4 u0 = src[0], u1 = src[1];
+            ++rd;
+            const uint32_t rc[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float2 qq = fadd2(make_float2(v[2 * i], v[2 * i + 1]), unpack_f16(rc[i]));
+              v[2 * i] = qq.x;
+              v[2 * i + 1] = qq.y;
+            }
+          }
+          uint32_t hy[8], ha[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {               // fp16 y, and v becomes it (as fp32)
+            hy[i] = pack_f16(v[2 * i], v[2 * i + 1]);
+            const float2 qq = unpack_f16(hy[i]);
+            v[2 * i] = qq.x;
+            v[2 * i + 1] = qq.y;
+          }
+          if (act) {
+            const int c = cmod ? nb % a.cout : nb;
+            if (chk) {
+              const bool good = snake16<true>(v, s_alpha + c, s_inv + c, ha);
+              if (!__all_sync(0xffffffffu, good || !live)) snake16_exact(v, s_alpha + c, s_inv + c, ha);   // rare
+            } else {
+              snake16<false>(v, s_alpha + c, s_inv + c, ha);
+            }
+          }
+          if (lane == 0) bulk_wait_read();            // this warp's last stores have read the staging
+          __syncwarp();
+          uint4* dr = reinterpret_cast<uint4*>(wst + 2048 + lane * 32);
+          uint4* dn = reinterpret_cast<uint4*>(wst + 3072 + lane * 32);
+          if (a.raw != nullptr) {
+            dr[0] = make_uint4(hy[0], hy[1], hy[2], hy[3]);
+            dr[1] = make_uint4(hy[4], hy[5], hy[6], hy[7]);
+          }
+          if (a.nxt != nullptr) {
+            const uint32_t* o = act ? ha : hy;
+            dn[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            dn[1] = make_uint4(o[4], o[5], o[6], o[7]);
+          }
+          fence_proxy_async_smem();                    // the staging writes, to the TMA engine
+          __syncwarp();
+          if (lane == 0) {
+            if (a.raw != nullptr) tma_store_3d(&tmO, wst + 2048, nb, tw, bw);
+            if (a.nxt != nullptr) tma_store_3d(&tmN, wst + 3072, nb, tw, bw);
+            bulk_commit();
           }
         }
-      } else {
-        __half* rawp = (a.raw != nullptr && live) ? a.raw + b * a.raw_bs + ts * a.raw_ts + n0 : nullptr;
-        __half* nxtp = (a.nxt != nullptr && live) ? a.nxt + b * a.nxt_bs + a.nxt_off + ts * a.N + n0 : nullptr;
-        for (; f < W; f += PARTS) {
-          int s2 = s, ch2 = ch + PARTS;       // the next item of this warp
-          while (ch2 >= nchunk) {
-            ch2 -= nchunk;
-            ++s2;
-          }
-          uint32_t rn[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-          if (resp != nullptr && f + PARTS < W) ld_global_v8(resp + s2 * res_sub + ch2 * 16, rn);
-          const int nb = n0 + ch * 16;
-          if (nb < a.N) {                     // warp-uniform: a unit's last tile may reach past N
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+      }
+      // residual boxes still in flight (after a timeout) land before the CTA ends; so do the stores
+      for (; rd < rq; ++rd) mbar_wait(&rbw[rd & 1], (rd >> 1) & 1, ERR_TIMEOUT_FULL, KERNEL_ID_CONV);
+      if (lane == 0) bulk_wait_all();
+    } else {
+      const long long res_sub = 128LL * a.res_ts, raw_sub = 128LL * a.raw_ts, nxt_sub = 128LL * a.N;
+      int it = 0;
+      for (int q = cid; q < iters; q += ncl, ++it) {
+        const int acc = it & 1, use = it >> 1;
+        int b0, t0, n0;
+        coords(tile_of(q), &b0, &t0, &n0);
+        const int b = b0 + rb;
+        const bool live = b < a.rows;
+        const long long ts = t0 + rt;
+        // the unit's items are dealt round robin over the warps of this lane quarter, the deal continuing from unit to
+        // unit (a warp left with fewer items of one unit takes more of the next)
+        int f = part - (it * W) % PARTS;
+        if (f < 0) f += PARTS;
+        int s = f / nchunk, ch = f - s * nchunk;
+        // this thread's elements of (sub-tile 0, chunk 0) of the unit; null where nothing is read or written
+        const __half* resp = (a.res != nullptr && live) ? a.res + b * a.res_bs + ts * a.res_ts + n0 : nullptr;
+        uint32_t rc[8] = {0, 0, 0, 0, 0, 0, 0, 0};   // residual of the current item: the first one's is requested
+        if (resp != nullptr && f < W) ld_global_v8(resp + s * res_sub + ch * 16, rc);   // before the accumulator wait
+        const bool ok = mbar_wait(&tfull[acc], use & 1, ERR_TIMEOUT_ACCUM, KERNEL_ID_CONV);
+        if (!ok) break;                         // (recorded; the MMA has stopped too)
+        tc_fence_after();
+        const uint32_t tbase = tmem + acc * a.sub * a.acc_cols + (uint32_t(quarter * 32) << 16);
+        if (a.audio != nullptr) {
+          for (int sb = part; sb < a.sub; sb += PARTS) {
             float v[16];
-            tmem_ld16(tbase + s * a.acc_cols + ch * 16, v);
-            if (a.bias != nullptr) {
-#pragma unroll
-              for (int i = 0; i < 16; i += 4) {
-                const float4 bv = *reinterpret_cast<const float4*>(s_bias + nb + i);
-                const float2 p0 = fadd2(make_float2(v[i], v[i + 1]), make_float2(bv.x, bv.y));
-                const float2 p1 = fadd2(make_float2(v[i + 2], v[i + 3]), make_float2(bv.z, bv.w));
-                v[i] = p0.x;
-                v[i + 1] = p0.y;
-                v[i + 2] = p1.x;
-                v[i + 3] = p1.y;
-              }
+            tmem_ld16(tbase + sb * a.acc_cols, v);
+            if (live) {
+              const float bias = a.bias != nullptr ? a.bias[0] : 0.f;
+              a.audio[(size_t)b * a.audio_bs + t0 + sb * 128 + rt] = tanhf(f16r(v[0] + bias));
             }
-            if (resp != nullptr) {
+          }
+        } else {
+          __half* rawp = (a.raw != nullptr && live) ? a.raw + b * a.raw_bs + ts * a.raw_ts + n0 : nullptr;
+          __half* nxtp = (a.nxt != nullptr && live) ? a.nxt + b * a.nxt_bs + a.nxt_off + ts * a.N + n0 : nullptr;
+          for (; f < W; f += PARTS) {
+            int s2 = s, ch2 = ch + PARTS;       // the next item of this warp
+            while (ch2 >= nchunk) {
+              ch2 -= nchunk;
+              ++s2;
+            }
+            uint32_t rn[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            if (resp != nullptr && f + PARTS < W) ld_global_v8(resp + s2 * res_sub + ch2 * 16, rn);
+            const int nb = n0 + ch * 16;
+            if (nb < a.N) {                     // warp-uniform: a unit's last tile may reach past N
+              float v[16];
+              tmem_ld16(tbase + s * a.acc_cols + ch * 16, v);
+              if (a.bias != nullptr) {
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float2 q = fadd2(make_float2(v[2 * i], v[2 * i + 1]), unpack_f16(rc[i]));
+                for (int i = 0; i < 16; i += 4) {
+                  const float4 bv = *reinterpret_cast<const float4*>(s_bias + nb + i);
+                  const float2 p0 = fadd2(make_float2(v[i], v[i + 1]), make_float2(bv.x, bv.y));
+                  const float2 p1 = fadd2(make_float2(v[i + 2], v[i + 3]), make_float2(bv.z, bv.w));
+                  v[i] = p0.x;
+                  v[i + 1] = p0.y;
+                  v[i + 2] = p1.x;
+                  v[i + 3] = p1.y;
+                }
+              }
+              if (resp != nullptr) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  const float2 q = fadd2(make_float2(v[2 * i], v[2 * i + 1]), unpack_f16(rc[i]));
+                  v[2 * i] = q.x;
+                  v[2 * i + 1] = q.y;
+                }
+              }
+              uint32_t hy[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {     // fp16 y, and v becomes it (as fp32)
+                hy[i] = pack_f16(v[2 * i], v[2 * i + 1]);
+                const float2 q = unpack_f16(hy[i]);
                 v[2 * i] = q.x;
                 v[2 * i + 1] = q.y;
               }
-            }
-            uint32_t hy[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {     // fp16 y, and v becomes it (as fp32)
-              hy[i] = pack_f16(v[2 * i], v[2 * i + 1]);
-              const float2 q = unpack_f16(hy[i]);
-              v[2 * i] = q.x;
-              v[2 * i + 1] = q.y;
-            }
-            if (rawp != nullptr) st_global_v8(rawp + s * raw_sub + ch * 16, hy);   // one 32-byte sector a thread
-            if (act) {
-              const int c = cmod ? nb % a.cout : nb;
-              uint32_t ha[8];
-              if (chk) {
-                const bool good = snake16<true>(v, s_alpha + c, s_inv + c, ha);
-                if (!__all_sync(0xffffffffu, good || !live)) snake16_exact(v, s_alpha + c, s_inv + c, ha);   // rare
-              } else {
-                snake16<false>(v, s_alpha + c, s_inv + c, ha);
+              if (rawp != nullptr) st_global_v8(rawp + s * raw_sub + ch * 16, hy);   // one 32-byte sector a thread
+              if (act) {
+                const int c = cmod ? nb % a.cout : nb;
+                uint32_t ha[8];
+                if (chk) {
+                  const bool good = snake16<true>(v, s_alpha + c, s_inv + c, ha);
+                  if (!__all_sync(0xffffffffu, good || !live)) snake16_exact(v, s_alpha + c, s_inv + c, ha);   // rare
+                } else {
+                  snake16<false>(v, s_alpha + c, s_inv + c, ha);
+                }
+                if (nxtp != nullptr) st_global_v8(nxtp + s * nxt_sub + ch * 16, ha);
+              } else if (nxtp != nullptr) {
+                st_global_v8(nxtp + s * nxt_sub + ch * 16, hy);
               }
-              if (nxtp != nullptr) st_global_v8(nxtp + s * nxt_sub + ch * 16, ha);
-            } else if (nxtp != nullptr) {
-              st_global_v8(nxtp + s * nxt_sub + ch * 16, hy);
             }
-          }
 #pragma unroll
-          for (int i = 0; i < 8; ++i) rc[i] = rn[i];
-          s = s2;
-          ch = ch2;
+            for (int i = 0; i < 8; ++i) rc[i] = rn[i];
+            s = s2;
+            ch = ch2;
+          }
         }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if constexpr (PAIR)                   // the pair's MMA warp (first CTA) waits for both CTAs' drains
-          mbar_arrive_cluster(dsmem_addr(smem_u32(&tempty[acc]), 0));
-        else
-          mbar_arrive(&tempty[acc]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (PAIR)                   // the pair's MMA warp (first CTA) waits for both CTAs' drains
+            mbar_arrive_cluster(dsmem_addr(smem_u32(&tempty[acc]), 0));
+          else
+            mbar_arrive(&tempty[acc]);
+        }
       }
     }
   }
@@ -762,15 +882,43 @@ static int conv_check_outputs(const ConvArgs& a) {
   return A8_OK;
 }
 
-int conv_launch(const ConvPlan* p, cudaStream_t s) {
-  int rc = conv_check_outputs(p->args);
+int conv_launch(const ConvPlan* p0, cudaStream_t s) {
+  int rc = conv_check_outputs(p0->args);
   if (rc) return rc;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = p->grid;
-  cfg.blockDim = dim3(CONV_THREADS);
-  const ConvArgs& a = p->args;
+  ConvPlan q = *p0;
+  ConvArgs& a = q.args;
   const int params = ((a.bias != nullptr ? (a.N + 3) / 4 * 4 : 0) + 2 * ((a.cout + 3) / 4 * 4)) * 4;
-  cfg.dynamicSmemBytes = p->smem + params;
+  // 1x1 convs with channel-contiguous rows and at least 32 steps a unit: the epilogue's I/O by TMA boxes (residual in,
+  // outputs out), paid for with a shallower (A, B) pipeline; anything that does not fit keeps the per-lane epilogue
+  CUtensorMap tmR = {}, tmO = {}, tmN = {};
+  a.etma = 0;
+  if (!a.slab && a.taps == 1 && a.sub == 1 && a.TT >= 32 && a.TT % 32 == 0 && a.audio == nullptr && a.N % 16 == 0 &&
+      a.N % a.ntile == 0 && (a.res == nullptr || a.res_ts == a.N) && (a.raw == nullptr || a.raw_ts == a.N)) {
+    const int stage_bytes = 128 * a.KC * 2 + a.ntile * a.KC * 2;
+    const int budget = 227 * 1024 - 1024 - CONV_BAR_BYTES - params - ETMA_BYTES;
+    const int st = std::min(a.stages, budget / stage_bytes);
+    const auto FP16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const auto NOSW = CU_TENSOR_MAP_SWIZZLE_NONE;
+    bool ok = st >= 2;
+    if (ok && a.res != nullptr)
+      ok = encode_map_3d(&tmR, a.res, FP16, 2, a.N, a.T, a.rows, (uint64_t)a.N * 2, (uint64_t)a.res_bs * 2, 16, 32, 1,
+                         NOSW) == A8_OK;
+    if (ok && a.raw != nullptr)
+      ok = encode_map_3d(&tmO, a.raw, FP16, 2, a.N, a.T, a.rows, (uint64_t)a.N * 2, (uint64_t)a.raw_bs * 2, 16, 32, 1,
+                         NOSW) == A8_OK;
+    if (ok && a.nxt != nullptr)
+      ok = encode_map_3d(&tmN, a.nxt + a.nxt_off, FP16, 2, a.N, a.T, a.rows, (uint64_t)a.N * 2,
+                         (uint64_t)a.nxt_bs * 2, 16, 32, 1, NOSW) == A8_OK;
+    if (ok) {
+      a.etma = 1;
+      a.stages = st;
+      q.smem = st * stage_bytes + 1024 + CONV_BAR_BYTES;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = q.grid;
+  cfg.blockDim = dim3(CONV_THREADS);
+  cfg.dynamicSmemBytes = q.smem + params + (a.etma ? ETMA_BYTES : 0);
   if (cfg.dynamicSmemBytes > 227 * 1024) return A8_ERR_SIZE;
   cfg.stream = s;
   cudaLaunchAttribute at[2];
@@ -783,19 +931,16 @@ int conv_launch(const ConvPlan* p, cudaStream_t s) {
   cfg.attrs = at;
   cfg.numAttrs = a.pair ? 2 : 1;
   ++g_launches;
-  auto run = [&](auto kern) {
-    static_assert(sizeof(kern) > 0, "");
-    return cudaLaunchKernelEx(&cfg, kern, p->tmX, p->tmW, p->args);
-  };
-  static bool attr[4] = {false, false, false, false};
-  const int v = (a.KC == 64 ? 0 : 2) + (a.pair ? 1 : 0);
-  void (*kern)(CUtensorMap, CUtensorMap, ConvArgs) =
-      v == 0 ? k_conv<64, false> : v == 1 ? k_conv<64, true> : v == 2 ? k_conv<32, false> : k_conv<32, true>;
+  using Kern = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, ConvArgs);
+  static bool attr[6] = {false, false, false, false, false, false};
+  const int v = (a.KC == 64 ? 0 : 3) + (a.pair ? 1 : a.etma ? 2 : 0);
+  const Kern table[6] = {k_conv<64, false, false>, k_conv<64, true, false>, k_conv<64, false, true>,
+                         k_conv<32, false, false>, k_conv<32, true, false>, k_conv<32, false, true>};
   if (!attr[v]) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(table[v], cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     attr[v] = true;
   }
-  const cudaError_t e = run(kern);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, table[v], q.tmX, q.tmW, tmR, tmO, tmN, a);
   return e == cudaSuccess ? A8_OK : A8_ERR_CUDA;
 }
 

@@ -156,8 +156,13 @@ def test_conv_vs_oracle(L, name, Cin, Cout, k, dil, trans, stride, snake, T, row
         y = R.hf(y)
         assert rel(got, y) <= 4e-3 and frac_equal(got, y) >= 0.95, (name, step)
         st = d.xin[:rows, :c.ctx].float().cpu()
-        flips = int((st != c.state[:rows]).sum())                 # one-ulp sin() differences, rare
-        assert flips <= max(2, st.numel() // 100) and rel(st, c.state[:rows]) <= 1e-3, (name, step, flips)
+        # the carried context is exactly the last ctx rows of (old context ; this step's activated rows): the shift
+        # moves bytes
+        assert torch.equal(st, torch.cat([xin_before, act], 1)[:, -c.ctx:]), (name, step)
+        # against the oracle's own state: one-ulp sin() differences (the host's vectorised fp32 sin and CUDA's sinf
+        # disagree on a few values in a hundred, more or fewer with the host array's alignment)
+        flips = int((st != c.state[:rows]).sum())
+        assert flips <= max(2, st.numel() // 40) and rel(st, c.state[:rows]) <= 1e-3, (name, step, flips)
 
 
 def test_conv_1x1_residual(L):
