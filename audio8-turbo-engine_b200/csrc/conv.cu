@@ -40,6 +40,7 @@ struct ConvArgs {
   int slab, R, na, nb;
   int resident;             // slab mode, one output tile: all taps x cblocks weight tiles (nb of them) stay loaded
   int pair;                 // slab mode, streamed weights: CTA pairs (k_conv<KC, true>), half of each weight tile a CTA
+  int wbox;                 // slab mode, streamed weights: one TMA box (and one ring slot) a channel block, every tap
   int etma;                 // 1x1 convs: residual in / outputs out by TMA boxes (k_conv<KC, false, true>)
   int sub;                  // 128-row sub-tiles a unit (slab mode: 2 share every weight tile; else 1)
   int hb;                   // slab rows a TMA box (a slab of R rows is ceil(R / hb) boxes)
@@ -165,7 +166,8 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   const uint32_t a_bytes = 128 * KC * 2, b_bytes = (PAIR ? a.ntile / 2 : a.ntile) * KC * 2;
   const uint32_t stage_bytes = a_bytes + b_bytes;
   // pipeline: `stages` slots of (A, B) -- or, in slab mode, na slab slots then nb weight slots
-  const uint32_t pipe_bytes = a.slab ? a.na * a.a_slot + a.nb * b_bytes : stages * stage_bytes;
+  const uint32_t bslot = a.wbox ? a.taps * b_bytes : b_bytes;   // a weight ring slot: one tap's tile, or every tap's
+  const uint32_t pipe_bytes = a.slab ? a.na * a.a_slot + a.nb * bslot : stages * stage_bytes;
   const int nbar = a.slab ? a.na + (a.resident ? 1 : a.nb) : stages;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + pipe_bytes);
   uint64_t* empty = full + nbar;
@@ -252,7 +254,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
     // of (channel block, tap) -- all of them loaded once and kept (a.resident), or streamed through a ring of nb
     // slots in the order the MMA uses them. The two producers never wait on each other.
     auto slotA = [&](int s) { return smem + s * a.a_slot; };
-    auto slotB = [&](int s) { return smem + a.na * a.a_slot + s * b_bytes; };
+    auto slotB = [&](int s) { return smem + a.na * a.a_slot + s * bslot; };
     uint64_t *fullA = full, *emptyA = empty, *fullB = full + a.na, *emptyB = empty + a.na;
     if (warp == 0 && lane == 0) {
       const uint64_t pol_x = policy_evict_first();
@@ -303,6 +305,20 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
           int b0, t0, n0;
           coords(tile_of(q), &b0, &t0, &n0);
           for (int c = 0; c < cblocks && ok; ++c) {
+            if (a.wbox) {                        // every tap's tile of channel block c in one box
+              if (!(ok = mbar_wait(&emptyB[sb], pb ^ 1u, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
+              if constexpr (PAIR) {
+                if (rank == 0) mbar_arrive_expect_tx(&fullB[sb], 2 * bslot);
+                tma_load_3d_pair(slotB(sb), &tmW, dsmem_addr(smem_u32(&fullB[sb]), 0), c * KC,
+                                 n0 + (int)rank * (a.ntile / 2), 0, pol_w);
+              } else {
+                mbar_arrive_expect_tx(&fullB[sb], bslot);
+                tma_load_3d(slotB(sb), &tmW, &fullB[sb], c * KC, n0, 0, pol_w);
+              }
+              ++qb;
+              advance(sb, pb, a.nb);
+              continue;
+            }
             for (int j = 0; j < a.taps; ++j) {
               if (!(ok = mbar_wait(&emptyB[sb], pb ^ 1u, ERR_TIMEOUT_EMPTY, KERNEL_ID_CONV))) break;
               if constexpr (PAIR) {              // this CTA's half of the tile's output channels
@@ -359,6 +375,30 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
             }
             __syncwarp();
             dBr += a.taps * b_step;
+          } else if (a.wbox) {                   // slot sb holds channel block c's tile for every tap
+            if (!(ok = mbar_wait_all(&fullB[sb], pb, ERR_TIMEOUT_FULL, KERNEL_ID_CONV))) break;
+            tc_fence_after();
+            if (elect_one()) {
+              uint64_t da_j = dA0 + sa * a_step, db = dB0 + sb * (bslot >> 4);
+              for (int j = 0; j < a.taps; ++j, da_j += tap_step, db += b_step) {
+                const uint32_t acc0 = (c | j) != 0;
+                if constexpr (PAIR) {
+                  umma_f16_pair(d0, da_j, db, idesc, acc0);
+#pragma unroll
+                  for (int k = 1; k < KC / 16; ++k) umma_f16_pair(d0, da_j + 2 * k, db + 2 * k, idesc, 1);
+                } else {
+                  umma_f16(d0, da_j, db, idesc, acc0);
+#pragma unroll
+                  for (int k = 1; k < KC / 16; ++k) umma_f16(d0, da_j + 2 * k, db + 2 * k, idesc, 1);
+                }
+              }
+              if constexpr (PAIR)
+                umma_commit_pair(&emptyB[sb]);
+              else
+                umma_commit(&emptyB[sb]);
+            }
+            __syncwarp();
+            advance(sb, pb, a.nb);
           } else {
             uint64_t da_j = dA0 + sa * a_step;   // tap j reads the slab from row j * dil
             for (int j = 0; j < a.taps; ++j, da_j += tap_step) {
@@ -828,14 +868,20 @@ int conv_plan(ConvPlan* p, const void* xin, int rows, int T, int Cin, int ctx, c
     } else {
       a.resident = 0;
       a.na = 2;
-      a.nb = std::min(16, (budget - a.na * (int)a.a_slot) / b_bytes);
-      if (a.nb < 2) return A8_ERR_SIZE;                      // (not reached with the decoder's shapes)
       // Streamed weights: CTA pairs, each CTA holding half of every weight tile (so the ring holds twice the MMA
       // work in the same bytes) and one 256-row MMA instruction doing both CTAs' rows. Measured on the k7 convs at
       // Cin 192 / 384: ~8 % faster; the 2-tap transposed conv is not (kept on single CTAs).
-      if (a.sub == 1 && a.ntile % 32 == 0 && taps > 2) {
-        a.pair = 1;
-        a.nb = std::min(24, (budget - a.na * (int)a.a_slot) / (b_bytes / 2));
+      a.pair = (a.sub == 1 && a.ntile % 32 == 0 && taps > 2) ? 1 : 0;
+      const int bb = a.pair ? b_bytes / 2 : b_bytes, room = budget - a.na * (int)a.a_slot;
+      // A TMA box costs ~270 ns of the SM's load engine whatever its size (measured: 96-row boxes stream 45 GB/s an
+      // SM, 192-row ones 90, one 84 KB box of 7 taps 165), so when two slots fit, a slot holds one channel block's
+      // tiles for every tap, loaded as one 3-D box; else a ring of one tap's tile a slot.
+      if (a.sub == 1 && room >= 2 * taps * bb) {
+        a.wbox = 1;
+        a.nb = std::min(4, room / (taps * bb));
+      } else {
+        a.nb = std::min(a.pair ? 24 : 16, room / bb);
+        if (a.nb < 2) return A8_ERR_SIZE;                    // (not reached with the decoder's shapes)
       }
     }
   }
@@ -843,8 +889,12 @@ int conv_plan(ConvPlan* p, const void* xin, int rows, int T, int Cin, int ctx, c
   int rc = encode_map_3d(&p->tmX, xin, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Cin, ctx + T, rows, (uint64_t)Cin * 2,
                          (uint64_t)(ctx + T) * Cin * 2, a.KC, a.slab ? a.hb : a.TT, a.slab ? 1 : a.TB, sw);
   if (rc) return rc;
-  rc = encode_map_2d(&p->tmW, w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)taps * Cin, N, (uint64_t)taps * Cin * 2,
-                     a.KC, a.pair ? a.ntile / 2 : a.ntile, sw);
+  if (a.wbox)   // W [N, taps * Cin] viewed as (channel within Cin, output row, tap): box {KC, rows, taps}, tap-major
+    rc = encode_map_3d(&p->tmW, w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Cin, N, taps, (uint64_t)taps * Cin * 2,
+                       (uint64_t)Cin * 2, a.KC, a.pair ? a.ntile / 2 : a.ntile, taps, sw);
+  else
+    rc = encode_map_2d(&p->tmW, w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)taps * Cin, N,
+                       (uint64_t)taps * Cin * 2, a.KC, a.pair ? a.ntile / 2 : a.ntile, sw);
   if (rc) return rc;
   static int sms = 0;
   if (sms == 0) {
@@ -859,8 +909,8 @@ int conv_plan(ConvPlan* p, const void* xin, int rows, int T, int Cin, int ctx, c
   } else {
     p->grid = dim3(std::min(total, sms));
   }
-  p->smem = (a.slab ? a.na * a.a_slot + a.nb * (a.pair ? b_bytes / 2 : b_bytes) : a.stages * stage_bytes) + 1024 +
-            CONV_BAR_BYTES;
+  const int bslot = (a.pair ? b_bytes / 2 : b_bytes) * (a.wbox ? taps : 1);
+  p->smem = (a.slab ? a.na * a.a_slot + a.nb * bslot : a.stages * stage_bytes) + 1024 + CONV_BAR_BYTES;
   return A8_OK;
 }
 
