@@ -152,7 +152,8 @@ __device__ __forceinline__ void snake16_exact(const float* v, const float* al_s,
 // and both loads complete bytes on the first CTA's barriers; the first CTA's MMA warp issues for the pair and its
 // commits arrive on both CTAs' barriers; each CTA's epilogue drains its own accumulator rows and arrives on the first
 // CTA's accumulator-drained barrier. Half the MMA instructions, half the weight bytes a CTA.
-// ETMA: 1x1 convs (no slab, one 128-step sub-tile, at least 32 steps a unit): each epilogue warp moves its item's 32
+// ETMA: 1x1 convs (no slab, one 128-step sub-tile, at least 32 steps a unit) and the single-CTA slab convs whose
+// weights stream by channel-block boxes (the transposed convs): each epilogue warp moves its item's 32
 // token rows x 16 channels by TMA through its own shared-memory staging -- the residual in (one item ahead), the raw
 // output and the next conv's input out -- a box of whole lines instead of 32 scattered 32-byte sectors a warp access.
 template <int KC, bool PAIR, bool ETMA>
@@ -632,7 +633,9 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
             v[2 * i + 1] = qq.y;
           }
           if (act) {
-            const int c = cmod ? nb % a.cout : nb;
+            int c = nb;
+            if (cmod)
+              while (c >= a.cout) c -= a.cout;   // nb < N = phases x cout
             if (chk) {
               const bool good = snake16<true>(v, s_alpha + c, s_inv + c, ha);
               if (!__all_sync(0xffffffffu, good || !live)) snake16_exact(v, s_alpha + c, s_inv + c, ha);   // rare
@@ -745,7 +748,9 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
               }
               if (rawp != nullptr) st_global_v8(rawp + s * raw_sub + ch * 16, hy);   // one 32-byte sector a thread
               if (act) {
-                const int c = cmod ? nb % a.cout : nb;
+                int c = nb;
+                if (cmod)
+                  while (c >= a.cout) c -= a.cout;   // nb < N = phases x cout
                 uint32_t ha[8];
                 if (chk) {
                   const bool good = snake16<true>(v, s_alpha + c, s_inv + c, ha);
@@ -940,16 +945,23 @@ int conv_launch(const ConvPlan* p0, cudaStream_t s) {
   const int params = ((a.bias != nullptr ? (a.N + 3) / 4 * 4 : 0) + 2 * ((a.cout + 3) / 4 * 4)) * 4;
   // 1x1 convs with channel-contiguous rows and at least 32 steps a unit: the epilogue's I/O by TMA boxes (residual in,
   // outputs out), paid for with a shallower (A, B) pipeline; anything that does not fit keeps the per-lane epilogue
+  // The same for slab convs whose weights stream by channel-block boxes on single CTAs (the transposed convs), paid
+  // for with fewer weight slots.
   CUtensorMap tmR = {}, tmO = {}, tmN = {};
   a.etma = 0;
-  if (!a.slab && a.taps == 1 && a.sub == 1 && a.TT >= 32 && a.TT % 32 == 0 && a.audio == nullptr && a.N % 16 == 0 &&
-      a.N % a.ntile == 0 && (a.res == nullptr || a.res_ts == a.N) && (a.raw == nullptr || a.raw_ts == a.N)) {
+  const bool eshape = a.sub == 1 && a.TT >= 32 && a.TT % 32 == 0 && a.audio == nullptr && a.N % 16 == 0 &&
+                      a.N % a.ntile == 0 && (a.res == nullptr || a.res_ts == a.N) && (a.raw == nullptr || a.raw_ts == a.N);
+  const bool eplain = !a.slab && a.taps == 1, eslab = a.slab && a.wbox && !a.pair && !a.resident;
+  if (eshape && (eplain || eslab)) {
     const int stage_bytes = 128 * a.KC * 2 + a.ntile * a.KC * 2;
     const int budget = 227 * 1024 - 1024 - CONV_BAR_BYTES - params - ETMA_BYTES;
-    const int st = std::min(a.stages, budget / stage_bytes);
+    const int bslot = a.taps * a.ntile * a.KC * 2;
+    const int st = eplain ? std::min(a.stages, budget / stage_bytes)
+                          : std::min(a.nb, (budget - a.na * (int)a.a_slot) / bslot);
+    const int nbar = eplain ? st : a.na + st;   // ring barriers + accumulator barriers + slots + residual barriers
     const auto FP16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const auto NOSW = CU_TENSOR_MAP_SWIZZLE_NONE;
-    bool ok = st >= 2;
+    bool ok = st >= 2 && (2 * nbar + 4) * 8 + 8 + 2 * CONV_EPI_WARPS * 8 <= CONV_BAR_BYTES;
     if (ok && a.res != nullptr)
       ok = encode_map_3d(&tmR, a.res, FP16, 2, a.N, a.T, a.rows, (uint64_t)a.N * 2, (uint64_t)a.res_bs * 2, 16, 32, 1,
                          NOSW) == A8_OK;
@@ -961,8 +973,13 @@ int conv_launch(const ConvPlan* p0, cudaStream_t s) {
                          (uint64_t)a.nxt_bs * 2, 16, 32, 1, NOSW) == A8_OK;
     if (ok) {
       a.etma = 1;
-      a.stages = st;
-      q.smem = st * stage_bytes + 1024 + CONV_BAR_BYTES;
+      if (eplain) {
+        a.stages = st;
+        q.smem = st * stage_bytes + 1024 + CONV_BAR_BYTES;
+      } else {
+        a.nb = st;
+        q.smem = a.na * a.a_slot + st * bslot + 1024 + CONV_BAR_BYTES;
+      }
     }
   }
   cudaLaunchConfig_t cfg = {};
