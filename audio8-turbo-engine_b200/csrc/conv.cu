@@ -86,28 +86,27 @@ __device__ __forceinline__ uint64_t umma_desc_sw64_row(uint32_t addr) {
   return ((uint64_t)((addr >> 4) & 0x3FFFu)) | (1ull << 16) | (32ull << 32) | (1ull << 46) | (4ull << 61);
 }
 
-// sin^2(t) for |t| < 2^21 without branches: t = k pi/2 + r with k = rint(2t/pi) (round-to-nearest by adding 1.5 2^23)
-// and r = t - k pi/2 by a two-term split of pi/2 (Cody-Waite reduction with fused multiply-adds); then
-// sin^2(r) = r^2 P(r^2) with P the Taylor series of (sin r / r)^2 = sum_n (-1)^n 2^(2n+1) r^(2n) / (2n+2)!, whose
-// seventh term is below 4e-9 for |r| <= pi/4, so six are kept; odd k swaps sin^2 for cos^2 = 1 - sin^2. Emulated in
-// fp32 with fused multiply-adds against a float64 sin^2 over 2e6 random t a range, the result stays within 1.2e-7
-// absolute for every |t| < 2^22 (the split's error grows as k 2^-48); the epilogue keeps it to |t| < 2^21.
-// Computed two at a time with packed fp32 instructions (each lane rounds as the scalar instruction would).
+// sin^2(t) for |t| < 2^21 without branches. sin^2 has period pi, so t = k pi + r with k = rint(t / pi) (round to
+// nearest by adding 1.5 2^23) and r = t - k pi by a two-term split of pi (Cody-Waite reduction with fused
+// multiply-adds); then sin^2(r) = u P(u), u = r^2, with P of degree 5 fitted to sin^2(sqrt u) / u over
+// u in [0, (pi/2 + 0.1)^2] (iteratively reweighted least squares on 6000 Chebyshev nodes toward the minimax of the
+// absolute error of u P; the 0.1 covers r past pi/2 when 1/pi's rounding moves k by one at large |t|). Emulated in fp32
+// with fused multiply-adds against a float64 sin^2 (tests/test_sin2_poly.py), the result stays within 2.5e-7
+// absolute for |t| < 2^21. Computed two at a time with packed fp32 instructions (each lane rounds as the scalar
+// instruction would); no quadrant select.
 constexpr float SIN2_RANGE = 2097152.f;
 __device__ __forceinline__ float2 sin2_reduced2(float2 t) {
-  const float2 big = ffma2(t, f2(0.636619772367581343f), f2(12582912.0f));
+  const float2 big = ffma2(t, f2(0.318309873342514038f), f2(12582912.0f));   // 1 / pi
   const float2 k = fsub2(big, f2(12582912.0f));
-  float2 r = ffma2(k, f2(-1.57079637050628662109375f), t);  // -(pi/2 rounded to fp32)
-  r = ffma2(k, f2(4.37113900018624283e-8f), r);             // -(pi/2 minus that)
+  float2 r = ffma2(k, f2(-3.14159274101257324f), t);   // -(pi rounded to fp32)
+  r = ffma2(k, f2(8.74227765734758577e-8f), r);        // -(pi minus that)
   const float2 u = fmul2(r, r);
-  float2 p = ffma2(f2(-4.27556185e-6f), u, f2(1.41093474e-4f));   // -2^11 / 12!, 2^9 / 10!
-  p = ffma2(p, u, f2(-3.17460317e-3f));                           // -2^7 / 8!
-  p = ffma2(p, u, f2(4.44444444e-2f));                            // 2^5 / 6!
-  p = ffma2(p, u, f2(-3.33333333e-1f));                           // -2^3 / 4!
-  p = ffma2(p, u, f2(1.0f));                                      // 2 / 2!
-  const float2 s2 = fmul2(u, p);
-  const float2 c2 = fsub2(f2(1.0f), s2);                          // odd k: cos^2 = 1 - sin^2
-  return make_float2((__float_as_uint(big.x) & 1u) ? c2.x : s2.x, (__float_as_uint(big.y) & 1u) ? c2.y : s2.y);
+  float2 p = ffma2(f2(-3.453945510e-06f), u, f2(1.381000038e-04f));
+  p = ffma2(p, u, f2(-3.169148928e-03f));
+  p = ffma2(p, u, f2(4.443938658e-02f));
+  p = ffma2(p, u, f2(-3.333311677e-01f));
+  p = ffma2(p, u, f2(9.999997020e-01f));
+  return fmul2(u, p);
 }
 
 // The next conv's input of 16 consecutive outputs: ha = fp16(y + inv sin^2(alpha y)) from the fp16-rounded y (as
@@ -688,8 +687,6 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
         int s = f / nchunk, ch = f - s * nchunk;
         // this thread's elements of (sub-tile 0, chunk 0) of the unit; null where nothing is read or written
         const __half* resp = (a.res != nullptr && live) ? a.res + b * a.res_bs + ts * a.res_ts + n0 : nullptr;
-        uint32_t rc[8] = {0, 0, 0, 0, 0, 0, 0, 0};   // residual of the current item: the first one's is requested
-        if (resp != nullptr && f < W) ld_global_v8(resp + s * res_sub + ch * 16, rc);   // before the accumulator wait
         const bool ok = mbar_wait(&tfull[acc], use & 1, ERR_TIMEOUT_ACCUM, KERNEL_ID_CONV);
         if (!ok) break;                         // (recorded; the MMA has stopped too)
         tc_fence_after();
@@ -712,8 +709,6 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
               ch2 -= nchunk;
               ++s2;
             }
-            uint32_t rn[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            if (resp != nullptr && f + PARTS < W) ld_global_v8(resp + s2 * res_sub + ch2 * 16, rn);
             const int nb = n0 + ch * 16;
             if (nb < a.N) {                     // warp-uniform: a unit's last tile may reach past N
               float v[16];
@@ -730,7 +725,9 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
                   v[i + 3] = p1.y;
                 }
               }
-              if (resp != nullptr) {
+              if (resp != nullptr) {            // (the decoder's residual convs take the TMA-box epilogue)
+                uint32_t rc[8];
+                ld_global_v8(resp + s * res_sub + ch * 16, rc);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                   const float2 q = fadd2(make_float2(v[2 * i], v[2 * i + 1]), unpack_f16(rc[i]));
@@ -763,8 +760,6 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
                 st_global_v8(nxtp + s * nxt_sub + ch * 16, hy);
               }
             }
-#pragma unroll
-            for (int i = 0; i < 8; ++i) rc[i] = rn[i];
             s = s2;
             ch = ch2;
           }
