@@ -11,10 +11,12 @@
 // Work unit = 128 token rows (TB batch rows x TT timesteps) x ntile output channels. The A tile of K block (tap j,
 // channel block c) is ONE 3-D TMA box {KC, TT, TB} at (c*KC, t0 + j*dil, b0) of xin -- the tap shift is a coordinate.
 // One CTA per SM loops over work units:
-//   warp 0      TMA producer: a ring of `stages` A+B slots
+//   warp 0      TMA producer: a ring of `stages` A+B slots (slab mode: the input slabs)
 //   warp 1      MMA issuer (tcgen05.mma kind::f16, fp16 x fp16 -> fp32) into one of two TMEM accumulators
-//   warps 2-9   epilogue: while the MMA fills one accumulator, these drain the other (tcgen05.ld 16 columns at a time;
-//               a lane quarter of TMEM is shared by two warps, which split the columns)
+//   warp 2      slab mode: the weight tiles
+//   warps 3-18  epilogue: while the MMA fills one accumulator, these drain the other (tcgen05.ld 16 columns at a
+//               time; a lane quarter of TMEM is shared by four warps, which deal its 16-column chunks round robin).
+//               19 warps put five on three of the SM's four register-file quarters: 96 registers a thread.
 // The epilogue writes, per output: the raw fp16 y (the residual stream), and/or the NEXT conv's input rows
 // snake(y) (x + inv * sin(alpha x)^2 on the fp16 y, stored fp16) straight into that conv's xin after its context --
 // so no separate activation pass -- or, for conv_out, tanh(fp16 y) into fp32 audio.
