@@ -963,7 +963,8 @@ int conv_launch(const ConvPlan* p0, cudaStream_t s) {
   CUtensorMap tmR = {}, tmO = {}, tmN = {};
   a.etma = 0;
   const bool eshape = a.sub == 1 && a.TT >= 32 && a.TT % 32 == 0 && a.audio == nullptr && a.N % 16 == 0 &&
-                      a.N % a.ntile == 0 && (a.res == nullptr || a.res_ts == a.N) && (a.raw == nullptr || a.raw_ts == a.N);
+                      a.N % a.ntile == 0 && (a.res == nullptr || a.res_ts == a.N) &&
+                      (a.raw == nullptr || a.raw_ts == a.N);
   const bool eplain = !a.slab && a.taps == 1, eslab = a.slab && a.wbox && !a.pair && !a.resident;
   if (eshape && (eplain || eslab)) {
     const int stage_bytes = 128 * a.KC * 2 + a.ntile * a.KC * 2;
