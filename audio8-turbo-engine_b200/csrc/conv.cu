@@ -838,6 +838,19 @@ static int conv_plan_kc(ConvPlan* p, const void* xin, int rows, int T, int Cin, 
   a.ntile = std::max(16, ((N + nt - 1) / nt + 15) / 16 * 16);
   a.n_tiles = (N + a.ntile - 1) / a.ntile;
   a.m_tiles = (T / a.TT) * ((rows + a.TB - 1) / a.TB);
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+  }
+  // A k > 1 conv outside slab mode with too few work units for the SMs (the first conv at T = 4: 36 units of 256
+  // columns) takes narrower output tiles: each SM then streams a smaller share of the weights
+  if (taps > 1 && !(a.TT == 128 && ctx <= 128))
+    while (a.ntile >= 128 && a.ntile % 32 == 0 && 2 * a.m_tiles * a.n_tiles <= sms) {
+      a.ntile /= 2;
+      a.n_tiles = (N + a.ntile - 1) / a.ntile;
+    }
   a.kb_total = taps * (Cin / a.KC);
   a.acc_cols = a.ntile <= 32 ? 32 : a.ntile <= 64 ? 64 : a.ntile <= 128 ? 128 : 256;
   const int stage_bytes = 128 * a.KC * 2 + a.ntile * a.KC * 2;
@@ -899,12 +912,6 @@ static int conv_plan_kc(ConvPlan* p, const void* xin, int rows, int T, int Cin, 
     rc = encode_map_2d(&p->tmW, w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)taps * Cin, N,
                        (uint64_t)taps * Cin * 2, a.KC, a.pair ? a.ntile / 2 : a.ntile, sw);
   if (rc) return rc;
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
-  }
   const int total = a.m_tiles * a.n_tiles;
   if (a.pair) {
     const int pairs = (a.m_tiles + 1) / 2 * a.n_tiles;
